@@ -1,0 +1,81 @@
+"""gmm_b200 -- B200-native (sm_100a) MoE grouped-GEMM forward.
+
+Drop-in for the reference's Python surface (reference
+``hopper_gmm_forward/__init__.py:59-88``)::
+
+    from gmm_b200 import hopper_gmm_fwd          # or: from hopper_gmm_forward import ...
+    d = hopper_gmm_fwd(a, b, batch_sizes)        # d[rows_e] = a[rows_e] @ b[e]
+
+The operator is registered as ``torch.ops.hopper_gmm_fwd.gmm`` (schema
+``gmm(Tensor A, Tensor B, Tensor batch_sizes, bool trans_b) -> Tensor``) by
+the in-tree ``_C.so``, loaded with ``torch.ops.load_library`` like the
+reference's extension (reference ``hopper_gmm_forward/__init__.py:19-46``);
+its fake (meta) implementation is registered here for ``torch.compile`` /
+export.  There is no CPU fallback: without the native library the call
+raises ``RuntimeError``.
+"""
+
+from __future__ import annotations
+
+import os
+import warnings
+
+import torch
+
+_PKG_DIR = os.path.dirname(os.path.abspath(__file__))
+_TORCH_OP = os.path.join(_PKG_DIR, "_C.so")
+_HAS_C = False
+
+
+def _load_c_ext() -> bool:
+    if not os.path.exists(_TORCH_OP):
+        return False
+    try:
+        torch.ops.load_library(_TORCH_OP)
+    except Exception as e:  # noqa: BLE001
+        warnings.warn(f"gmm_b200: failed to load {_TORCH_OP}: {e}", RuntimeWarning)
+        return False
+    return True
+
+
+if _load_c_ext():
+    _HAS_C = True
+else:
+    warnings.warn("gmm_b200._C not built; run `python -m gmm_b200.build`. "
+                  f"No _C.so found in {_PKG_DIR}", RuntimeWarning)
+
+
+def hopper_gmm_fwd(a: torch.Tensor,
+                   b: torch.Tensor,
+                   batch_sizes: torch.Tensor,
+                   trans_b: bool = False) -> torch.Tensor:
+    """Forward-only grouped GEMM on B200 (sm_100a).
+
+    Args:
+        a: ``[num_tokens, dim]`` contiguous CUDA, fp32/bf16/fp16.
+        b: ``[num_experts, dim, dim_out]`` (or ``[num_experts, dim_out, dim]``
+           if ``trans_b=True``) contiguous CUDA, same dtype as ``a``.
+        batch_sizes: ``[num_experts]`` int64 tensor on CPU; rows
+           ``[sum(batch_sizes[:e]), sum(batch_sizes[:e+1]))`` of ``a`` belong
+           to expert ``e`` and ``sum(batch_sizes)`` must equal ``num_tokens``.
+        trans_b: ``b`` holds each expert's matrix transposed. For fp32 the
+           products run as three TF32 tensor-core passes (near-fp32 accuracy).
+
+    Returns:
+        ``[num_tokens, dim_out]`` tensor, same dtype/device as ``a``:
+        ``out[rows_e] = a[rows_e] @ (b[e].T if trans_b else b[e])``.
+    """
+    if not _HAS_C:
+        raise RuntimeError("gmm_b200._C is not available. Build with `python -m gmm_b200.build`.")
+    return torch.ops.hopper_gmm_fwd.gmm(a, b, batch_sizes, trans_b)
+
+
+if _HAS_C:
+    @torch.library.register_fake("hopper_gmm_fwd::gmm")
+    def _hopper_gmm_fwd_fake(a, b, batch_sizes, trans_b):
+        num_tokens = a.shape[0]
+        n = b.shape[1] if trans_b else b.shape[2]
+        return torch.empty(num_tokens, n, dtype=a.dtype, device=a.device)
+
+
+__all__ = ["hopper_gmm_fwd"]

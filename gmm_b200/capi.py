@@ -1,0 +1,98 @@
+"""ctypes binding of the C ABI in ``include/gmm_sm100.h`` (``libgmm_sm100.so``).
+
+This is what a non-torch caller binds; the tests use it to drive the kernels
+through the C ABI directly.  Pointers are passed as integers (e.g.
+``tensor.data_ptr()``), streams as ``torch.cuda.current_stream().cuda_stream``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+_PKG_DIR = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG_DIR, "libgmm_sm100.so")
+
+GMM_DTYPE_F32, GMM_DTYPE_BF16, GMM_DTYPE_F16 = 0, 1, 2
+
+# Every symbol the header declares, with its ctypes signature.
+_SIGNATURES = {
+    "gmm_sm100_errstr": (ctypes.c_char_p, [ctypes.c_int]),
+    "gmm_sm100_last_error": (ctypes.c_char_p, []),
+    "gmm_sm100_check_device": (ctypes.c_int, [ctypes.c_int]),
+    "gmm_sm100_workspace_size": (ctypes.c_size_t, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                                                   ctypes.c_int64, ctypes.c_int64, ctypes.c_int,
+                                                   ctypes.c_int]),
+    "gmm_sm100_forward": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                         ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                         ctypes.c_int64, ctypes.c_int, ctypes.c_int,
+                                         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
+                                         ctypes.c_void_p]),
+    "gmm_sm100_device_error": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int), ctypes.c_int]),
+}
+
+_lib = None
+
+
+def load():
+    """Load ``libgmm_sm100.so`` (raises ``OSError`` if it was not built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise OSError(f"{LIB_PATH} not built; run `python -m gmm_b200.build`")
+        lib = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+    return _lib
+
+
+class GmmError(RuntimeError):
+    def __init__(self, status, detail):
+        super().__init__(f"{detail} (status {status})")
+        self.status = status
+
+
+def _check(rc):
+    if rc != 0:
+        lib = load()
+        raise GmmError(rc, lib.gmm_sm100_last_error().decode() or lib.gmm_sm100_errstr(rc).decode())
+
+
+def dtype_code(torch_dtype) -> int:
+    import torch
+    return {torch.float32: GMM_DTYPE_F32, torch.bfloat16: GMM_DTYPE_BF16,
+            torch.float16: GMM_DTYPE_F16}[torch_dtype]
+
+
+def workspace_size(batch_sizes, num_tokens, dim, dim_out, dtype, trans_b) -> int:
+    import numpy as np
+    bs = np.ascontiguousarray(np.asarray(batch_sizes, dtype=np.int64))
+    return int(load().gmm_sm100_workspace_size(bs.ctypes.data, bs.shape[0], num_tokens, dim, dim_out,
+                                               dtype, int(bool(trans_b))))
+
+
+def forward(a, b, batch_sizes, d, trans_b=False, workspace=None, stream=None):
+    """Run ``gmm_sm100_forward`` on torch CUDA tensors through the C ABI (no torch op)."""
+    import numpy as np
+    import torch
+    bs = np.ascontiguousarray(np.asarray(batch_sizes, dtype=np.int64))
+    dtype = dtype_code(a.dtype)
+    dim = a.shape[1]
+    dim_out = b.shape[1] if trans_b else b.shape[2]
+    need = workspace_size(bs, a.shape[0], dim, dim_out, dtype, trans_b)
+    if need and workspace is None:
+        workspace = torch.empty(need, dtype=torch.uint8, device=a.device)
+    s = torch.cuda.current_stream(a.device).cuda_stream if stream is None else stream
+    _check(load().gmm_sm100_forward(a.data_ptr(), b.data_ptr(), bs.ctypes.data, bs.shape[0],
+                                    a.shape[0], dim, dim_out, dtype, int(bool(trans_b)),
+                                    d.data_ptr(), workspace.data_ptr() if need else None, need, s))
+    return d
+
+
+def device_error(clear=True) -> int:
+    v = ctypes.c_int(0)
+    _check(load().gmm_sm100_device_error(ctypes.byref(v), int(bool(clear))))
+    return v.value

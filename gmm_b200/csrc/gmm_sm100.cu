@@ -1,0 +1,748 @@
+// gmm_sm100.cu -- persistent grouped-GEMM forward for B200 (sm_100a) and its C ABI.
+//
+// Replaces the reference's CUTLASS sm_90a grouped GEMM
+// (reference csrc/hopper_gmm_forward.cu:67-138 kernel configuration,
+//  :230-325 launcher, :372-486 host entry) with a hand-written kernel:
+//
+//   * one persistent CTA per SM walks a static (group, m-tile, n-tile) tile
+//     list built from the host batch_sizes; zero-row experts own no tiles;
+//   * warp 0 (one lane) streams A and B tiles with TMA into a 4-stage
+//     shared-memory ring (128-byte swizzle);
+//   * warp 1 (one lane) issues tcgen05.mma (M=128, N=256, K=16 for bf16/fp16;
+//     M=128, N=128, K=8 with three TF32 products for fp32) into one of two
+//     TMEM accumulators;
+//   * warps 4-7 drain the other accumulator (tcgen05.ld), convert to the
+//     output type and store rows that belong to the tile's expert -- rows past
+//     an expert's segment are never written, which keeps output placement exact.
+//
+// A is addressed through one 2D tensor map over all T rows (a tile of expert
+// g starts at row off_g + 128 m); B through one 3D tensor map whose outer
+// coordinate is the expert.  No per-expert descriptors, no TMA multicast.
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "gmm_sm100.h"
+#include "sm100_ptx.cuh"
+
+namespace gmm_sm100 {
+
+// Device-side error word: set by a CTA whose bounded wait ran out.
+__device__ int g_device_error = 0;
+
+constexpr int kInlineGroups = 1024;  // groups whose table travels in the kernel parameters
+constexpr int kMBlock = 16;          // m-tiles per raster block (L2 reuse of B columns)
+constexpr int kThreads = 256;        // 8 warps: TMA, MMA, TMEM alloc, idle, 4x epilogue
+
+struct __align__(64) GmmParams {
+  CUtensorMap tmap_a;   // A, or A_hi for fp32
+  CUtensorMap tmap_b;   // B, or B_hi for fp32
+  CUtensorMap tmap_a2;  // A_lo (fp32 only)
+  CUtensorMap tmap_b2;  // B_lo (fp32 only)
+  void* d;
+  const int32_t* ext_table;  // device table when num_groups > kInlineGroups
+  long long ldd;
+  int num_groups;
+  int n_tiles;
+  int k_blocks;
+  int total_tiles;
+  int dim_out;
+  int pad_;
+  // Table of the non-empty groups, laid out as
+  //   row_off[G+1] | tile_off[G+1] | expert[G]
+  // row_off: first row of group g in A/D (row_off[G] = T);
+  // tile_off: prefix sum of m-tiles (ceil(m_g / 128));
+  // expert: index of the expert (B slice) of group g.
+  int32_t inline_table[3 * kInlineGroups + 2];
+};
+
+enum Kind : int { kKindTf32x3 = 0, kKindBf16 = 1, kKindF16 = 2 };
+
+template <int kKind, bool kBMnMajor>
+struct Cfg {
+  static constexpr bool kTf32 = (kKind == kKindTf32x3);
+  static constexpr int kElem = kTf32 ? 4 : 2;
+  static constexpr int BM = 128;
+  static constexpr int BN = kTf32 ? 128 : 256;
+  static constexpr int BK = 128 / kElem;  // one 128-byte swizzle row of K
+  static constexpr int kStages = kTf32 ? 3 : 4;
+  static constexpr int kUmmaK = 32 / kElem;  // K per tcgen05.mma: 16 (16-bit), 8 (tf32)
+  static constexpr int kKSteps = BK / kUmmaK;
+  static constexpr int kParts = kTf32 ? 2 : 1;  // hi/lo operand copies
+  static constexpr int kABytes = BM * BK * kElem;
+  static constexpr int kBBytes = BN * BK * kElem;
+  static constexpr int kStageBytes = kParts * (kABytes + kBBytes);
+  static constexpr int kTmemCols = 2 * BN;  // double-buffered fp32 accumulator
+  static constexpr uint32_t kIdesc =
+      make_idesc(kTf32 ? 2u : (kKind == kKindBf16 ? 1u : 0u), kBMnMajor, BM, BN);
+  static constexpr int kBarBytes = 256;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kBarBytes + 1024;
+  static_assert(!(kTf32 && kBMnMajor), "fp32 B is staged K-major by the split pre-pass");
+  static_assert(kABytes % 1024 == 0 && kBBytes % 1024 == 0, "swizzle atoms need 1 KB alignment");
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+};
+
+struct TableView {
+  const int32_t* row_off;
+  const int32_t* tile_off;
+  const int32_t* expert;
+};
+
+struct Tile {
+  int row0;    // first row of the tile in A / D
+  int rows;    // rows of the tile that belong to its expert (1..128)
+  int n0;      // first output column
+  int expert;  // B slice
+};
+
+template <int BM, int BN>
+__device__ __forceinline__ Tile decode_tile(const TableView& t, int n_tiles, int tile, int& g) {
+  // Groups are visited in increasing order by every CTA, so a forward scan
+  // from the previous group finds the owner in amortised O(1).
+  while (tile >= t.tile_off[g + 1] * n_tiles) ++g;
+  const int mt = t.tile_off[g + 1] - t.tile_off[g];
+  const int local = tile - t.tile_off[g] * n_tiles;
+  // Raster: blocks of up to kMBlock m-tiles; inside a block m varies fastest so
+  // the CTAs working on one B column panel run at the same time (L2 reuse).
+  const int blk = local / (kMBlock * n_tiles);
+  const int r = local - blk * kMBlock * n_tiles;
+  const int h = min(kMBlock, mt - blk * kMBlock);
+  const int m = blk * kMBlock + r % h;
+  const int n = r / h;
+  Tile out;
+  out.row0 = t.row_off[g] + m * BM;
+  out.rows = min(BM, t.row_off[g + 1] - out.row0);
+  out.n0 = n * BN;
+  out.expert = t.expert[g];
+  return out;
+}
+
+// Bounded wait used while draining after an abort: ignores the abort flag.
+__device__ __forceinline__ void mbar_wait_drain(uint32_t bar, uint32_t parity) {
+  const unsigned long long t0 = global_timer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (global_timer_ns() - t0 > kWaitTimeoutNs) return;
+  }
+}
+
+template <typename OutT>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi);
+
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
+  __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+template <int kKind, bool kBMnMajor>
+__global__ void __launch_bounds__(kThreads, 1) gmm_persistent_kernel(const __grid_constant__ GmmParams p) {
+  using C = Cfg<kKind, kBMnMajor>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
+  uint64_t* full_bar = bars;                       // TMA -> MMA
+  uint64_t* empty_bar = bars + C::kStages;         // MMA -> TMA
+  uint64_t* tfull_bar = bars + 2 * C::kStages;     // MMA -> epilogue (2 accumulators)
+  uint64_t* tempty_bar = bars + 2 * C::kStages + 2;  // epilogue -> MMA
+  uint64_t* drain_bar = bars + 2 * C::kStages + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * C::kStages + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(smem_u32(full_bar + s), 1);
+      mbar_init(smem_u32(empty_bar + s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(tfull_bar + a), 1);
+      mbar_init(smem_u32(tempty_bar + a), 4);
+    }
+    mbar_init(smem_u32(drain_bar), 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&p.tmap_a);
+    prefetch_tmap(&p.tmap_b);
+    if (C::kTf32) {
+      prefetch_tmap(&p.tmap_a2);
+      prefetch_tmap(&p.tmap_b2);
+    }
+  }
+  if (warp == 2) {
+    tmem_alloc(smem_u32(tmem_slot), C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int32_t* tab = p.ext_table ? p.ext_table : p.inline_table;
+  TableView tv;
+  tv.row_off = tab;
+  tv.tile_off = tab + p.num_groups + 1;
+  tv.expert = tab + 2 * (p.num_groups + 1);
+  const int n_tiles = p.n_tiles;
+  const int k_blocks = p.k_blocks;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued[C::kStages];
+      for (int s = 0; s < C::kStages; ++s) issued[s] = 0;
+      bool ok = true;
+      int g = 0;
+      for (int tile = blockIdx.x; ok && tile < p.total_tiles; tile += gridDim.x) {
+        const Tile t = decode_tile<C::BM, C::BN>(tv, n_tiles, tile, g);
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(smem_u32(empty_bar + stage), phase ^ 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = smem_u32(full_bar + stage);
+          mbar_arrive_expect_tx(fb, C::kStageBytes);
+          uint8_t* sa = smem + stage * C::kStageBytes;
+          uint8_t* sb = sa + C::kParts * C::kABytes;
+          const int k0 = kb * C::BK;
+          tma_load_2d(smem_u32(sa), &p.tmap_a, fb, k0, t.row0);
+          if (C::kTf32) {
+            tma_load_2d(smem_u32(sa + C::kABytes), &p.tmap_a2, fb, k0, t.row0);
+            tma_load_3d(smem_u32(sb), &p.tmap_b, fb, k0, t.n0, t.expert);
+            tma_load_3d(smem_u32(sb + C::kBBytes), &p.tmap_b2, fb, k0, t.n0, t.expert);
+          } else if (kBMnMajor) {
+            // B[e] is [K, N] (N contiguous): BN/64 panels of [BK rows][64 cols].
+#pragma unroll
+            for (int c = 0; c < C::BN / 64; ++c)
+              tma_load_3d(smem_u32(sb + c * (C::BK * 128)), &p.tmap_b, fb, t.n0 + 64 * c, k0,
+                          t.expert);
+          } else {
+            tma_load_3d(smem_u32(sb), &p.tmap_b, fb, k0, t.n0, t.expert);
+          }
+          issued[stage]++;
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        // Let every copy already in flight land before the CTA can exit.
+        for (int s = 0; s < C::kStages; ++s)
+          if (issued[s] > 0) mbar_wait_drain(smem_u32(full_bar + s), (issued[s] - 1) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int local = 0;
+      for (int tile = blockIdx.x; ok && tile < p.total_tiles; tile += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(smem_u32(tempty_bar + acc), acc_phase ^ 1, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * C::BN;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(smem_u32(full_bar + stage), phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * C::kStageBytes);
+          const uint32_t sb = sa + C::kParts * C::kABytes;
+#pragma unroll
+          for (int ks = 0; ks < C::kKSteps; ++ks) {
+            const uint32_t acc_flag = (kb | ks) != 0 ? 1u : 0u;
+            const uint64_t adesc = make_sw128_desc(sa + ks * 32, 16, 1024);
+            uint64_t bdesc;
+            if (kBMnMajor)
+              bdesc = make_sw128_desc(sb + ks * C::kUmmaK * 128, C::BK * 128, 1024);
+            else
+              bdesc = make_sw128_desc(sb + ks * 32, 16, 1024);
+            if (C::kTf32) {
+              const uint64_t adesc_lo = make_sw128_desc(sa + C::kABytes + ks * 32, 16, 1024);
+              const uint64_t bdesc_lo = make_sw128_desc(sb + C::kBBytes + ks * 32, 16, 1024);
+              mma_tf32_ss(d_tmem, adesc, bdesc, C::kIdesc, acc_flag);    // hi * hi
+              mma_tf32_ss(d_tmem, adesc, bdesc_lo, C::kIdesc, 1u);      // hi * lo
+              mma_tf32_ss(d_tmem, adesc_lo, bdesc, C::kIdesc, 1u);      // lo * hi
+            } else {
+              mma_f16_ss(d_tmem, adesc, bdesc, C::kIdesc, acc_flag);
+            }
+          }
+          mma_commit(smem_u32(empty_bar + stage));  // frees the stage once these MMAs retire
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit(smem_u32(tfull_bar + acc));  // accumulator ready for the epilogue
+      }
+      // Retire every MMA this thread issued before TMEM can be released.
+      mma_commit(smem_u32(drain_bar));
+      mbar_wait_drain(smem_u32(drain_bar), 0);
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int r = quarter * 32 + lane;
+    int g = 0;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(smem_u32(tfull_bar + acc), acc_phase, abort_flag)) break;
+      tc_fence_after();
+      const Tile t = decode_tile<C::BM, C::BN>(tv, n_tiles, tile, g);
+      if (quarter * 32 < t.rows) {  // warp-uniform: some row of this quarter is live
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * C::BN;
+        const bool row_live = r < t.rows;
+        const long long drow = static_cast<long long>(t.row0 + r) * p.ldd;
+#pragma unroll 1
+        for (int c = 0; c < C::BN / 32; ++c) {
+          const int col = t.n0 + c * 32;
+          if (col >= p.dim_out) break;  // warp-uniform
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(taddr + c * 32, v);
+          tmem_wait_ld();
+          if (!row_live) continue;
+          if (C::kTf32) {
+            float* out = reinterpret_cast<float*>(p.d) + drow + col;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              if (col + q * 4 < p.dim_out) {
+                uint4 pk = make_uint4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                *reinterpret_cast<uint4*>(out + q * 4) = pk;
+              }
+            }
+          } else {
+            using OutT = typename std::conditional<kKind == kKindBf16, __nv_bfloat16, __half>::type;
+            OutT* out = reinterpret_cast<OutT*>(p.d) + drow + col;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              if (col + q * 8 < p.dim_out) {
+                uint4 pk;
+                pk.x = pack2<OutT>(__uint_as_float(v[8 * q + 0]), __uint_as_float(v[8 * q + 1]));
+                pk.y = pack2<OutT>(__uint_as_float(v[8 * q + 2]), __uint_as_float(v[8 * q + 3]));
+                pk.z = pack2<OutT>(__uint_as_float(v[8 * q + 4]), __uint_as_float(v[8 * q + 5]));
+                pk.w = pack2<OutT>(__uint_as_float(v[8 * q + 6]), __uint_as_float(v[8 * q + 7]));
+                *reinterpret_cast<uint4*>(out + q * 8) = pk;
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(tempty_bar + acc));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+  if (threadIdx.x == 0 && *abort_flag) atomicCAS(&g_device_error, 0, GMM_ERR_DEVICE_TIMEOUT);
+}
+
+// ------------------------------------------------------------------ fp32 pre-pass
+// Splits x into a TF32-exact high part (low 13 mantissa bits cleared) and the
+// fp32 remainder, so that three TF32 products hi*hi + hi*lo + lo*hi recover
+// close to fp32 accuracy.  Non-finite values pass through in hi with lo = 0.
+__device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
+  if (isfinite(x)) {
+    hi = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+    lo = x - hi;
+  } else {
+    hi = x;
+    lo = 0.0f;
+  }
+}
+
+__global__ void split_tf32_kernel(const float4* __restrict__ x, float4* __restrict__ hi,
+                                  float4* __restrict__ lo, long long n4) {
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n4;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const float4 v = x[i];
+    float4 h, l;
+    split_tf32(v.x, h.x, l.x);
+    split_tf32(v.y, h.y, l.y);
+    split_tf32(v.z, h.z, l.z);
+    split_tf32(v.w, h.w, l.w);
+    hi[i] = h;
+    lo[i] = l;
+  }
+}
+
+// b[e] is [K, N]; writes hi[e], lo[e] as [N, K] (K contiguous) for K-major TF32 operands.
+__global__ void split_tf32_transpose_kernel(const float* __restrict__ b, float* __restrict__ hi,
+                                            float* __restrict__ lo, int K, int N) {
+  __shared__ float tile[32][33];
+  const long long e_off = static_cast<long long>(blockIdx.z) * K * N;
+  const int n0 = blockIdx.x * 32, k0 = blockIdx.y * 32;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int k = k0 + i, n = n0 + threadIdx.x;
+    tile[i][threadIdx.x] = (k < K && n < N) ? b[e_off + static_cast<long long>(k) * N + n] : 0.f;
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int n = n0 + i, k = k0 + threadIdx.x;
+    if (n < N && k < K) {
+      float h, l;
+      split_tf32(tile[threadIdx.x][i], h, l);
+      const long long o = e_off + static_cast<long long>(n) * K + k;
+      hi[o] = h;
+      lo[o] = l;
+    }
+  }
+}
+
+}  // namespace gmm_sm100
+
+// =====================================================================  host side
+namespace {
+
+using namespace gmm_sm100;
+
+thread_local std::string t_last_error;
+
+int fail(int code, const std::string& msg) {
+  t_last_error = msg;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(GMM_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_tiled() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = []() -> PFN_cuTensorMapEncodeTiled_v12000 {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault,
+                                         &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }();
+  return fn;
+}
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceInfo {
+  std::atomic<int> state{0};  // 0 unknown, 1 ok, 2 wrong arch
+  int sm_count = 0;
+  int cc_major = 0, cc_minor = 0;
+  std::atomic<unsigned> smem_attr_set{0};  // bit per kernel variant
+};
+DeviceInfo g_dev[kMaxDevices];
+std::mutex g_dev_mu;
+
+int device_info(int dev, DeviceInfo** out) {
+  if (dev < 0 || dev >= kMaxDevices) return fail(GMM_ERR_INVALID_ARGUMENT, "device index out of range");
+  DeviceInfo& d = g_dev[dev];
+  if (d.state.load(std::memory_order_acquire) == 0) {
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    if (d.state.load() == 0) {
+      cudaError_t e;
+      if ((e = cudaDeviceGetAttribute(&d.cc_major, cudaDevAttrComputeCapabilityMajor, dev)) != cudaSuccess ||
+          (e = cudaDeviceGetAttribute(&d.cc_minor, cudaDevAttrComputeCapabilityMinor, dev)) != cudaSuccess ||
+          (e = cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+        return cuda_fail(e, "cudaDeviceGetAttribute");
+      d.state.store((d.cc_major == 10 && d.cc_minor == 0) ? 1 : 2, std::memory_order_release);
+    }
+  }
+  *out = &d;
+  if (d.state.load() != 1)
+    return fail(GMM_ERR_ARCH, "gmm_sm100 requires a compute capability 10.0 (B200) GPU, got " +
+                                  std::to_string(d.cc_major) + "." + std::to_string(d.cc_minor));
+  return GMM_OK;
+}
+
+size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+struct Plan {
+  int num_groups = 0;
+  int n_tiles = 0, k_blocks = 0, total_tiles = 0;
+  std::vector<int32_t> table;
+  size_t table_bytes = 0;    // device table bytes (0 when inline)
+  size_t split_bytes = 0;    // fp32 hi/lo staging
+  size_t a_part = 0, b_part = 0;
+};
+
+int elem_size(int dtype) { return dtype == GMM_DTYPE_F32 ? 4 : 2; }
+
+int make_plan(const int64_t* bs, int64_t E, int64_t T, int64_t K, int64_t N, int dtype, Plan& pl) {
+  if (E < 0 || T < 0 || K < 0 || N < 0) return fail(GMM_ERR_INVALID_ARGUMENT, "negative size");
+  if (E > 0 && !bs) return fail(GMM_ERR_INVALID_ARGUMENT, "batch_sizes is null");
+  if (dtype != GMM_DTYPE_F32 && dtype != GMM_DTYPE_BF16 && dtype != GMM_DTYPE_F16)
+    return fail(GMM_ERR_DTYPE, "Unsupported dtype: only FP32 / BF16 / FP16 are supported");
+  const int64_t BM = 128;
+  const int64_t BN = dtype == GMM_DTYPE_F32 ? 128 : 256;
+  const int64_t BK = dtype == GMM_DTYPE_F32 ? 32 : 64;
+  int64_t sum = 0, groups = 0, mtiles = 0;
+  for (int64_t e = 0; e < E; ++e) {
+    if (bs[e] < 0) return fail(GMM_ERR_INVALID_ARGUMENT, "batch_sizes[" + std::to_string(e) + "] is negative");
+    sum += bs[e];
+    if (bs[e] > 0) {
+      ++groups;
+      mtiles += (bs[e] + BM - 1) / BM;
+    }
+  }
+  if (sum != T)
+    return fail(GMM_ERR_BATCH_SUM, "Sum of batch_sizes (" + std::to_string(sum) +
+                                       ") must equal A.size(0) (" + std::to_string(T) + ")");
+  if (T > INT32_MAX - 256 || K > INT32_MAX || N > INT32_MAX || E > INT32_MAX)
+    return fail(GMM_ERR_TOO_LARGE, "a dimension exceeds the int32 coordinate range");
+  const int64_t n_tiles = (N + BN - 1) / BN;
+  const int64_t total = mtiles * n_tiles;
+  if (total > INT32_MAX) return fail(GMM_ERR_TOO_LARGE, "too many output tiles");
+  pl.num_groups = static_cast<int>(groups);
+  pl.n_tiles = static_cast<int>(n_tiles);
+  pl.k_blocks = static_cast<int>((K + BK - 1) / BK);
+  pl.total_tiles = static_cast<int>(total);
+  pl.table.assign(3 * groups + 2, 0);
+  int32_t* row_off = pl.table.data();
+  int32_t* tile_off = row_off + groups + 1;
+  int32_t* expert = tile_off + groups + 1;
+  int64_t row = 0, tiles = 0, g = 0;
+  for (int64_t e = 0; e < E; ++e) {
+    if (bs[e] > 0) {
+      row_off[g] = static_cast<int32_t>(row);
+      tile_off[g] = static_cast<int32_t>(tiles);
+      expert[g] = static_cast<int32_t>(e);
+      ++g;
+      tiles += (bs[e] + BM - 1) / BM;
+    }
+    row += bs[e];
+  }
+  row_off[groups] = static_cast<int32_t>(row);
+  tile_off[groups] = static_cast<int32_t>(tiles);
+  pl.table_bytes = groups > kInlineGroups ? round_up(pl.table.size() * sizeof(int32_t), 256) : 0;
+  if (dtype == GMM_DTYPE_F32) {
+    pl.a_part = round_up(static_cast<size_t>(T) * K * 4, 256);
+    pl.b_part = round_up(static_cast<size_t>(E) * K * N * 4, 256);
+    pl.split_bytes = 2 * pl.a_part + 2 * pl.b_part;
+  }
+  return GMM_OK;
+}
+
+int encode(CUtensorMap* m, CUtensorMapDataType type, int rank, const void* ptr,
+           const cuuint64_t* dims, const cuuint64_t* strides_bytes, const cuuint32_t* box) {
+  auto fn = encode_tiled();
+  if (!fn) return fail(GMM_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUresult r = fn(m, type, rank, const_cast<void*>(ptr), dims, strides_bytes, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(GMM_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
+  return GMM_OK;
+}
+
+template <int kKind, bool kMn>
+int launch_variant(const GmmParams& prm, int grid, cudaStream_t stream, DeviceInfo* di, int bit) {
+  using C = Cfg<kKind, kMn>;
+  auto kern = gmm_persistent_kernel<kKind, kMn>;
+  if (!(di->smem_attr_set.load() & (1u << bit))) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+    di->smem_attr_set.fetch_or(1u << bit);
+  }
+  kern<<<grid, kThreads, C::kSmemBytes, stream>>>(prm);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "gmm kernel launch");
+  return GMM_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+extern "C" {
+
+const char* gmm_sm100_errstr(int status) {
+  switch (status) {
+    case GMM_OK: return "ok";
+    case GMM_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case GMM_ERR_BATCH_SUM: return "sum of batch_sizes does not match the number of rows";
+    case GMM_ERR_DTYPE: return "unsupported dtype";
+    case GMM_ERR_ALIGNMENT: return "misaligned pointer or row pitch";
+    case GMM_ERR_ARCH: return "unsupported GPU architecture (needs sm_100)";
+    case GMM_ERR_CUDA: return "CUDA error";
+    case GMM_ERR_WORKSPACE: return "workspace too small";
+    case GMM_ERR_TOO_LARGE: return "problem too large";
+    case GMM_ERR_DEVICE_TIMEOUT: return "device-side wait timed out";
+    default: return "unknown status";
+  }
+}
+
+const char* gmm_sm100_last_error(void) { return t_last_error.c_str(); }
+
+int gmm_sm100_check_device(int device) {
+  DeviceInfo* di = nullptr;
+  return device_info(device, &di);
+}
+
+size_t gmm_sm100_workspace_size(const int64_t* batch_sizes, int64_t num_experts, int64_t num_tokens,
+                                int64_t dim, int64_t dim_out, int dtype, int trans_b) {
+  (void)trans_b;
+  Plan pl;
+  if (make_plan(batch_sizes, num_experts, num_tokens, dim, dim_out, dtype, pl) != GMM_OK) return 0;
+  return pl.split_bytes + pl.table_bytes;
+}
+
+int gmm_sm100_forward(const void* A, const void* B, const int64_t* batch_sizes, int64_t num_experts,
+                      int64_t num_tokens, int64_t dim, int64_t dim_out, int dtype, int trans_b,
+                      void* D, void* workspace, size_t workspace_bytes, void* stream_ptr) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  Plan pl;
+  int rc = make_plan(batch_sizes, num_experts, num_tokens, dim, dim_out, dtype, pl);
+  if (rc != GMM_OK) return rc;
+  const int64_t T = num_tokens, K = dim, N = dim_out, E = num_experts;
+  if (T == 0 || N == 0) return GMM_OK;  // nothing to write
+  if (!D) return fail(GMM_ERR_INVALID_ARGUMENT, "D is null");
+  const int es = elem_size(dtype);
+  if (!aligned16(D)) return fail(GMM_ERR_ALIGNMENT, "D must be 16-byte aligned");
+  if ((N * es) % 16 != 0)
+    return fail(GMM_ERR_ALIGNMENT, "dim_out * element size must be a multiple of 16 bytes, got dim_out=" +
+                                       std::to_string(N));
+  int dev = 0;
+  cudaError_t ce = cudaGetDevice(&dev);
+  if (ce != cudaSuccess) return cuda_fail(ce, "cudaGetDevice");
+  DeviceInfo* di = nullptr;
+  if ((rc = device_info(dev, &di)) != GMM_OK) return rc;
+  if (K == 0) {  // empty contraction: D = 0
+    ce = cudaMemsetAsync(D, 0, static_cast<size_t>(T) * N * es, stream);
+    return ce == cudaSuccess ? GMM_OK : cuda_fail(ce, "cudaMemsetAsync");
+  }
+  if (!A || !B) return fail(GMM_ERR_INVALID_ARGUMENT, "A or B is null");
+  if (!aligned16(A) || !aligned16(B)) return fail(GMM_ERR_ALIGNMENT, "A and B must be 16-byte aligned");
+  if ((K * es) % 16 != 0)
+    return fail(GMM_ERR_ALIGNMENT, "dim * element size must be a multiple of 16 bytes, got dim=" +
+                                       std::to_string(K));
+  const size_t need = pl.split_bytes + pl.table_bytes;
+  if (need > 0 && (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255u)))
+    return fail(GMM_ERR_WORKSPACE, "workspace needs " + std::to_string(need) + " bytes (256-byte aligned), got " +
+                                       std::to_string(workspace_bytes));
+
+  static_assert(sizeof(GmmParams) <= 32764, "kernel parameter limit");
+  GmmParams prm;
+  std::memset(&prm, 0, sizeof(prm));
+  prm.d = D;
+  prm.ldd = N;
+  prm.num_groups = pl.num_groups;
+  prm.n_tiles = pl.n_tiles;
+  prm.k_blocks = pl.k_blocks;
+  prm.total_tiles = pl.total_tiles;
+  prm.dim_out = static_cast<int>(N);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  if (pl.table_bytes == 0) {
+    std::memcpy(prm.inline_table, pl.table.data(), pl.table.size() * sizeof(int32_t));
+    prm.ext_table = nullptr;
+  } else {
+    uint8_t* tdev = ws + pl.split_bytes;
+    ce = cudaMemcpyAsync(tdev, pl.table.data(), pl.table.size() * sizeof(int32_t), cudaMemcpyHostToDevice, stream);
+    if (ce != cudaSuccess) return cuda_fail(ce, "cudaMemcpyAsync(table)");
+    prm.ext_table = reinterpret_cast<const int32_t*>(tdev);
+  }
+
+  const cuuint64_t uT = T, uK = K, uN = N, uE = E;
+  if (dtype == GMM_DTYPE_F32) {
+    float* a_hi = reinterpret_cast<float*>(ws);
+    float* a_lo = reinterpret_cast<float*>(ws + pl.a_part);
+    float* b_hi = reinterpret_cast<float*>(ws + 2 * pl.a_part);
+    float* b_lo = reinterpret_cast<float*>(ws + 2 * pl.a_part + pl.b_part);
+    const long long n4a = T * K / 4;
+    const int sgrid = static_cast<int>(std::min<long long>((n4a + 255) / 256, 4LL * di->sm_count));
+    split_tf32_kernel<<<std::max(sgrid, 1), 256, 0, stream>>>(
+        reinterpret_cast<const float4*>(A), reinterpret_cast<float4*>(a_hi), reinterpret_cast<float4*>(a_lo), n4a);
+    if (trans_b) {
+      const long long n4b = E * K * N / 4;
+      const int bgrid = static_cast<int>(std::min<long long>((n4b + 255) / 256, 4LL * di->sm_count));
+      split_tf32_kernel<<<std::max(bgrid, 1), 256, 0, stream>>>(
+          reinterpret_cast<const float4*>(B), reinterpret_cast<float4*>(b_hi), reinterpret_cast<float4*>(b_lo), n4b);
+    } else {
+      dim3 tg(static_cast<unsigned>((N + 31) / 32), static_cast<unsigned>((K + 31) / 32), static_cast<unsigned>(E));
+      split_tf32_transpose_kernel<<<tg, dim3(32, 8), 0, stream>>>(static_cast<const float*>(B), b_hi, b_lo,
+                                                                  static_cast<int>(K), static_cast<int>(N));
+    }
+    ce = cudaGetLastError();
+    if (ce != cudaSuccess) return cuda_fail(ce, "split pre-pass launch");
+    const cuuint64_t adims[2] = {uK, uT}, astr[1] = {uK * 4};
+    const cuuint32_t abox[2] = {32, 128};
+    const cuuint64_t bdims[3] = {uK, uN, uE}, bstr[2] = {uK * 4, uN * uK * 4};
+    const cuuint32_t bbox[3] = {32, 128, 1};
+    if ((rc = encode(&prm.tmap_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a_hi, adims, astr, abox)) ||
+        (rc = encode(&prm.tmap_a2, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a_lo, adims, astr, abox)) ||
+        (rc = encode(&prm.tmap_b, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, b_hi, bdims, bstr, bbox)) ||
+        (rc = encode(&prm.tmap_b2, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, b_lo, bdims, bstr, bbox)))
+      return rc;
+  } else {
+    const CUtensorMapDataType tt =
+        dtype == GMM_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const cuuint64_t adims[2] = {uK, uT}, astr[1] = {uK * 2};
+    const cuuint32_t abox[2] = {64, 128};
+    if ((rc = encode(&prm.tmap_a, tt, 2, A, adims, astr, abox))) return rc;
+    if (trans_b) {  // B[e] is [N, K], K contiguous
+      const cuuint64_t bdims[3] = {uK, uN, uE}, bstr[2] = {uK * 2, uN * uK * 2};
+      const cuuint32_t bbox[3] = {64, 256, 1};
+      if ((rc = encode(&prm.tmap_b, tt, 3, B, bdims, bstr, bbox))) return rc;
+    } else {  // B[e] is [K, N], N contiguous
+      const cuuint64_t bdims[3] = {uN, uK, uE}, bstr[2] = {uN * 2, uK * uN * 2};
+      const cuuint32_t bbox[3] = {64, 64, 1};
+      if ((rc = encode(&prm.tmap_b, tt, 3, B, bdims, bstr, bbox))) return rc;
+    }
+  }
+
+  const int grid = std::max(1, std::min(pl.total_tiles, di->sm_count));
+  if (dtype == GMM_DTYPE_F32) return launch_variant<kKindTf32x3, false>(prm, grid, stream, di, 0);
+  if (dtype == GMM_DTYPE_BF16)
+    return trans_b ? launch_variant<kKindBf16, false>(prm, grid, stream, di, 1)
+                   : launch_variant<kKindBf16, true>(prm, grid, stream, di, 2);
+  return trans_b ? launch_variant<kKindF16, false>(prm, grid, stream, di, 3)
+                 : launch_variant<kKindF16, true>(prm, grid, stream, di, 4);
+}
+
+int gmm_sm100_device_error(int* status_out, int clear) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyFromSymbol(g_device_error)");
+  if (clear) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyToSymbol(g_device_error)");
+  }
+  if (status_out) *status_out = v;
+  return GMM_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,95 @@
+/*
+ * gmm_sm100.h -- C ABI of the B200 (sm_100a) grouped-GEMM forward.
+ *
+ * One library, libgmm_sm100.so, exports these symbols.  Signatures carry only
+ * plain pointers, integers and sizes (no C++ or torch types), so the library
+ * can be bound from C, C++ (the torch operator in gmm_b200/csrc/torch_op.cpp),
+ * Python ctypes, or any other FFI.  No exception crosses the boundary: every
+ * entry point returns 0 or a negative gmm_status code.
+ *
+ * Semantics (the reference's forward, reference csrc/hopper_gmm_forward.h:9-25):
+ *   A : [num_tokens, dim]            row-major, device memory
+ *   B : [num_experts, dim, dim_out]  row-major (trans_b = 0), or
+ *       [num_experts, dim_out, dim]  row-major (trans_b = 1), device memory
+ *   batch_sizes : [num_experts] int64 in HOST memory, sum == num_tokens
+ *   D : [num_tokens, dim_out]        row-major, device memory, same dtype as A
+ * For each expert e with rows [off_e, off_e + batch_sizes[e]):
+ *   D[rows] = A[rows] @ B[e]        (B[e]^T when trans_b)
+ * accumulated in fp32.  Zero-row experts are skipped.  fp32 inputs are
+ * multiplied on the tensor cores as three TF32 products (hi*hi + hi*lo +
+ * lo*hi) which gives close to fp32 accuracy.
+ */
+#ifndef GMM_SM100_H_
+#define GMM_SM100_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element types (A, B and D share one). */
+enum gmm_dtype {
+  GMM_DTYPE_F32 = 0,  /* fp32 in/out, 3xTF32 tensor-core products */
+  GMM_DTYPE_BF16 = 1, /* bf16 in/out, fp32 accumulate */
+  GMM_DTYPE_F16 = 2   /* fp16 in/out, fp32 accumulate */
+};
+
+/* Status codes. */
+enum gmm_status {
+  GMM_OK = 0,
+  GMM_ERR_INVALID_ARGUMENT = -1, /* null pointer, negative size, bad shape */
+  GMM_ERR_BATCH_SUM = -2,        /* sum(batch_sizes) != num_tokens */
+  GMM_ERR_DTYPE = -3,            /* dtype not one of gmm_dtype */
+  GMM_ERR_ALIGNMENT = -4,        /* pointer or row pitch not 16-byte aligned */
+  GMM_ERR_ARCH = -5,             /* device is not compute capability 10.0 */
+  GMM_ERR_CUDA = -6,             /* a CUDA runtime / driver call failed */
+  GMM_ERR_WORKSPACE = -7,        /* workspace missing or smaller than required */
+  GMM_ERR_TOO_LARGE = -8,        /* a size exceeds the kernel's index range */
+  GMM_ERR_DEVICE_TIMEOUT = -9    /* a kernel wait ran out (see gmm_sm100_device_error) */
+};
+
+/* Human-readable text for a status code (static storage). */
+const char* gmm_sm100_errstr(int status);
+
+/* Detail of the last failure on the calling thread (thread-local storage). */
+const char* gmm_sm100_last_error(void);
+
+/* GMM_OK if `device` is a compute-capability 10.0 (B200-class) GPU.
+ * Replaces the reference's compute-capability check
+ * (reference csrc/hopper_gmm_forward.cu:389-397). */
+int gmm_sm100_check_device(int device);
+
+/* Bytes of device workspace gmm_sm100_forward needs for this problem; 0 for
+ * bf16/fp16 with at most 1024 non-empty experts.  Replaces the reference's
+ * workspace sizing (reference csrc/hopper_gmm_forward.cu:210-222, 411-427). */
+size_t gmm_sm100_workspace_size(const int64_t* batch_sizes, int64_t num_experts,
+                                int64_t num_tokens, int64_t dim, int64_t dim_out, int dtype,
+                                int trans_b);
+
+/* The grouped-GEMM forward: validates, builds the tile schedule from the host
+ * batch_sizes and launches the persistent tcgen05 kernel on `stream` (a
+ * cudaStream_t; NULL = legacy default stream).  Asynchronous: returns once the
+ * work is enqueued.  `workspace` must hold gmm_sm100_workspace_size() bytes,
+ * 256-byte aligned (may be NULL when that size is 0); it must stay allocated
+ * until the work on `stream` completes.  Every row of D is written (D need
+ * not be initialised).  Replaces the reference's entry point
+ * hpc_ops_hopper::hopper_gmm_forward (reference csrc/hopper_gmm_forward.cu:372-486)
+ * and its launcher CutlassGroupedGemm (reference csrc/hopper_gmm_forward.cu:230-325). */
+int gmm_sm100_forward(const void* A, const void* B, const int64_t* batch_sizes,
+                      int64_t num_experts, int64_t num_tokens, int64_t dim, int64_t dim_out,
+                      int dtype, int trans_b, void* D, void* workspace, size_t workspace_bytes,
+                      void* stream);
+
+/* Reads (and with clear != 0, resets) the device-side error word of the
+ * current device: 0, or a gmm_status recorded by a kernel whose bounded wait
+ * ran out.  Synchronises the device.  No reference counterpart (the
+ * reference kernel has no device-side error path). */
+int gmm_sm100_device_error(int* status_out, int clear);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GMM_SM100_H_ */

@@ -1,0 +1,98 @@
+"""The drop-in boundary, checked without a GPU: op schema, fake impl, Python
+signature, the C ABI's exported symbols and its host-side validation."""
+
+import ctypes
+import inspect
+import os
+import re
+
+import numpy as np
+import pytest
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "gmm_sm100.h")
+
+
+def test_header_symbols_exported():
+    from gmm_b200 import capi
+    lib = capi.load()
+    declared = set(re.findall(r"\b(gmm_sm100_\w+)\s*\(", open(HEADER).read()))
+    assert declared, "no declarations parsed"
+    for name in declared:
+        assert hasattr(lib, name), f"{name} declared in the header but not exported"
+    assert declared == set(capi._SIGNATURES), "ctypes binding out of sync with the header"
+
+
+def test_op_schema_matches_reference():
+    import gmm_b200  # noqa: F401
+    schema = str(torch.ops.hopper_gmm_fwd.gmm.default._schema)
+    assert schema == ("hopper_gmm_fwd::gmm(Tensor A, Tensor B, Tensor batch_sizes, bool trans_b) -> Tensor")
+
+
+def test_python_signature_matches_reference():
+    from gmm_b200 import hopper_gmm_fwd
+    import hopper_gmm_forward
+    sig = inspect.signature(hopper_gmm_fwd)
+    assert list(sig.parameters) == ["a", "b", "batch_sizes", "trans_b"]
+    assert sig.parameters["trans_b"].default is False
+    assert hopper_gmm_forward.hopper_gmm_fwd is hopper_gmm_fwd
+    assert hopper_gmm_forward.__all__ == ["hopper_gmm_fwd"]
+
+
+@pytest.mark.parametrize("trans_b", [False, True])
+def test_fake_impl_shapes(trans_b):
+    import gmm_b200  # noqa: F401
+    from torch._subclasses.fake_tensor import FakeTensorMode
+    with FakeTensorMode():
+        bs = torch.tensor([128, 0, 384])
+        a = torch.empty(512, 64, dtype=torch.float16, device="cuda")
+        b = torch.empty(3, 96, 64, dtype=torch.float16, device="cuda") if trans_b else \
+            torch.empty(3, 64, 96, dtype=torch.float16, device="cuda")
+        out = torch.ops.hopper_gmm_fwd.gmm(a, b, bs, trans_b)
+        assert tuple(out.shape) == (512, 96) and out.dtype == torch.float16
+        assert out.device.type == "cuda"
+
+
+def test_cpu_tensors_have_no_kernel():
+    """Like the reference, only the CUDA dispatch key is implemented: no CPU fallback."""
+    import gmm_b200  # noqa: F401
+    with pytest.raises(NotImplementedError):
+        torch.ops.hopper_gmm_fwd.gmm(torch.zeros(4, 8), torch.zeros(1, 8, 8), torch.tensor([4]), False)
+
+
+def _cabi_forward(bs, T, dim=16, dim_out=16, dtype=1, trans_b=0):
+    from gmm_b200 import capi
+    lib = capi.load()
+    arr = np.asarray(bs, dtype=np.int64)
+    # Non-null dummy pointers: validation fails before any CUDA call.
+    rc = lib.gmm_sm100_forward(16, 16, arr.ctypes.data, len(bs), T, dim, dim_out, dtype, trans_b,
+                               16, None, 0, None)
+    return rc, lib.gmm_sm100_last_error().decode()
+
+
+def test_cabi_validates_on_host():
+    rc, msg = _cabi_forward([3, 4], 10)
+    assert rc == -2 and msg == "Sum of batch_sizes (7) must equal A.size(0) (10)"
+    rc, msg = _cabi_forward([3, -1], 2)
+    assert rc == -1 and "negative" in msg
+    rc, msg = _cabi_forward([3], 3, dtype=7)
+    assert rc == -3 and msg.startswith("Unsupported dtype")
+    rc, _ = _cabi_forward([0, 0], 0)  # T = 0: nothing to do, no CUDA call
+    assert rc == 0
+
+
+def test_cabi_errstr_and_workspace():
+    from gmm_b200 import capi
+    lib = capi.load()
+    for code in range(0, -10, -1):
+        assert lib.gmm_sm100_errstr(code) not in (None, b"unknown status")
+    assert lib.gmm_sm100_errstr(-100) == b"unknown status"
+    # bf16/fp16 with a small table: no workspace
+    assert capi.workspace_size([64] * 8, 512, 128, 256, capi.GMM_DTYPE_BF16, False) == 0
+    # fp32: hi/lo copies of A and B (each 256-byte rounded)
+    ws = capi.workspace_size([64] * 8, 512, 128, 256, capi.GMM_DTYPE_F32, False)
+    assert ws == 2 * 512 * 128 * 4 + 2 * 8 * 128 * 256 * 4
+    # more than 1024 non-empty experts: the table moves to the workspace
+    ws = capi.workspace_size([1] * 2000, 2000, 64, 64, capi.GMM_DTYPE_F16, True)
+    assert ws == ((3 * 2000 + 2) * 4 + 255) // 256 * 256

@@ -1,0 +1,207 @@
+"""Parity of the sm_100a grouped-GEMM kernels with the reference's math.
+
+The reference's own correctness test (reference tests/test_forward.py) is the
+model: the same shape table, dtypes and layouts, compared with per-expert
+fp32-accumulated matmuls -- here the pinned CPU oracle and the reference's
+own ``ref_gmm`` golden outputs.  Tolerances (rtol = atol): bf16 1.6e-2,
+fp16 2e-3, fp32 5e-3; row placement is checked bit-exactly.
+"""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from cases import make_case_inputs
+from gpu_util import check_rows, golden, golden_values, sampled_subproblem
+
+pytestmark = pytest.mark.gpu
+
+GOLD, CASES = golden()
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _device():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import gmm_b200  # noqa: F401  (loads the op)
+    torch.cuda.set_device(0)
+    yield
+    from gmm_b200 import capi
+    assert capi.device_error(clear=True) == 0, "a kernel recorded a device-side timeout"
+
+
+def _fwd(a, b, bs, trans_b):
+    from gmm_b200 import hopper_gmm_fwd
+    return hopper_gmm_fwd(a, b, bs, trans_b=trans_b)
+
+
+@pytest.mark.parametrize("case", CASES, ids=[c["name"] for c in CASES])
+def test_golden_case(case):
+    a, b, bs = make_case_inputs(case)
+    out = _fwd(a.cuda(), b.cuda(), bs, case["trans_b"])
+    torch.cuda.synchronize()
+    assert out.shape == (a.shape[0], b.shape[1] if case["trans_b"] else b.shape[2])
+    assert out.dtype == a.dtype
+    tol = oracle.TOLERANCE[case["dtype"]]
+    # 1) against the reference's own ref_gmm outputs (sampled rows)
+    rows = GOLD[case["name"] + "__rows"]
+    got = out.float().cpu().numpy()
+    ok, nbad, err = oracle.allclose_report(got[rows], golden_values(GOLD, case), tol)
+    assert ok, f"vs reference ref_gmm: {nbad} bad, max err {err:.3e}"
+    # 2) against the oracle on every row
+    want = oracle.round_to(oracle.gmm_oracle_c(a, b, bs, case["trans_b"]), case["dtype"])
+    ok, nbad, err = oracle.allclose_report(got, want, tol)
+    assert ok, f"vs oracle: {nbad} bad, max err {err:.3e}"
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("trans_b", [False, True])
+def test_placement_is_exact(dtype, trans_b):
+    """B[e] = (e+1) * I: every output row must be exactly (e+1) * its input row."""
+    bs = [5, 0, 300, 1, 129, 0, 128, 17, 0, 64]
+    dim = 256
+    T = sum(bs)
+    g = torch.Generator().manual_seed(3)
+    a = torch.randint(-8, 9, (T, dim), generator=g).to(dtype)
+    eye = torch.eye(dim)
+    b = torch.stack([(e + 1) * eye for e in range(len(bs))]).to(dtype)
+    out = _fwd(a.cuda(), b.cuda(), torch.tensor(bs), trans_b).cpu()
+    scale = torch.repeat_interleave(torch.arange(1, len(bs) + 1, dtype=torch.float32), torch.tensor(bs))
+    want = (a.float() * scale[:, None]).to(dtype)
+    assert torch.equal(out, want)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_canary_rows_untouched(dtype):
+    """Drive the C ABI into the middle of a NaN-filled buffer: nothing outside D is written."""
+    from gmm_b200 import capi
+    bs = [3, 0, 200, 0, 70]
+    T, dim, dim_out, pad = sum(bs), 136, 264, 37
+    a = torch.randn(T, dim, device="cuda").to(dtype)
+    b = torch.randn(len(bs), dim, dim_out, device="cuda").to(dtype)
+    big = torch.full((T + 2 * pad, dim_out), float("nan"), device="cuda", dtype=dtype)
+    d = big[pad:pad + T]
+    capi.forward(a, b, bs, d, trans_b=False)
+    torch.cuda.synchronize()
+    assert torch.isnan(big[:pad]).all() and torch.isnan(big[pad + T:]).all()
+    assert not torch.isnan(d).any()
+    check_rows(d, a.cpu(), b.cpu(), bs, False, oracle.dtype_name(dtype), "canary")
+
+
+def test_more_groups_than_inline_table():
+    """1500 non-empty experts: the tile table goes through the device workspace."""
+    E = 1500
+    g = torch.Generator().manual_seed(11)
+    bs = torch.randint(1, 5, (E,), generator=g)
+    bs[::7] = 0
+    T, dim, dim_out = int(bs.sum()), 64, 128
+    a = torch.randn(T, dim, generator=g).to(torch.bfloat16)
+    b = (torch.randn(E, dim_out, dim, generator=g) / 8).to(torch.bfloat16)
+    out = _fwd(a.cuda(), b.cuda(), bs, True)
+    want = oracle.round_to(oracle.gmm_oracle_np(a, b, bs, True), "bf16")
+    ok, nbad, err = oracle.allclose_report(out.float().cpu().numpy(), want, 1.6e-2)
+    assert ok, (nbad, err)
+
+
+def test_degenerate_sizes():
+    dev = "cuda"
+    # all experts empty -> T = 0
+    out = _fwd(torch.empty(0, 64, device=dev, dtype=torch.bfloat16),
+               torch.randn(3, 64, 32, device=dev).bfloat16(), torch.zeros(3, dtype=torch.int64), False)
+    assert out.shape == (0, 32)
+    # dim = 0 -> zeros
+    out = _fwd(torch.empty(5, 0, device=dev, dtype=torch.float16),
+               torch.empty(2, 0, 16, device=dev, dtype=torch.float16), torch.tensor([2, 3]), False)
+    assert out.shape == (5, 16) and (out == 0).all()
+    # one row, one expert, tiny dims (M, N and K tails all at once)
+    a = torch.randn(1, 8, device=dev).bfloat16()
+    b = torch.randn(1, 8, 8, device=dev).bfloat16()
+    out = _fwd(a, b, torch.tensor([1]), False)
+    check_rows(out, a.cpu(), b.cpu(), [1], False, "bf16", "1x8x8")
+
+
+def test_reference_error_messages():
+    dev = "cuda"
+    a = torch.randn(10, 64, device=dev).bfloat16()
+    b = torch.randn(2, 64, 32, device=dev).bfloat16()
+    with pytest.raises(RuntimeError, match=r"Sum of batch_sizes \(9\) must equal A.size\(0\) \(10\)"):
+        _fwd(a, b, torch.tensor([4, 5]), False)
+    with pytest.raises(RuntimeError, match="batch_sizes must be a 1D CPU int64 tensor"):
+        _fwd(a, b, torch.tensor([4, 6], device=dev), False)
+    with pytest.raises(RuntimeError, match="A and B must have the same dtype"):
+        _fwd(a, b.half(), torch.tensor([4, 6]), False)
+    with pytest.raises(RuntimeError, match=r"B.size\(0\) must equal num_experts"):
+        _fwd(a, b, torch.tensor([4, 3, 3]), False)
+    with pytest.raises(RuntimeError, match=r"B.size\(1\) must equal A.size\(1\) \(dim\)"):
+        _fwd(a, torch.randn(2, 32, 64, device=dev).bfloat16(), torch.tensor([4, 6]), False)
+    with pytest.raises(RuntimeError, match="Unsupported dtype"):
+        _fwd(a.double(), b.double(), torch.tensor([4, 6]), False)
+    with pytest.raises(RuntimeError, match="A must be a contiguous CUDA tensor"):
+        _fwd(torch.randn(64, 10, device=dev).bfloat16().t(), b, torch.tensor([4, 6]), False)
+
+
+def test_deterministic_and_stream_ordered():
+    a = torch.randn(3000, 512, device="cuda").bfloat16()
+    b = (torch.randn(4, 512, 768, device="cuda") / 16).bfloat16()
+    bs = torch.tensor([1000, 0, 1500, 500])
+    ref = _fwd(a, b, bs, False)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        outs = [_fwd(a, b, bs, False) for _ in range(3)]
+    s.synchronize()
+    for o in outs:
+        assert torch.equal(o, ref)
+
+
+# ------------------------------------------------------------ workload configs
+def _config_inputs(cid):
+    from gmm_b200.configs import CONFIGS, batch_sizes_for, make_inputs
+    cfg = CONFIGS[cid]
+    bs = batch_sizes_for(cfg)
+    if cid == 1:
+        a, b = make_inputs(cfg, "cpu")
+        a, b = a.cuda(), b.cuda()
+    else:
+        a, b = make_inputs(cfg, "cuda")
+    return cfg, bs, a, b
+
+
+@pytest.mark.parametrize("cid", [1, 2, 3, 4, 5])
+def test_config_parity(cid):
+    cfg, bs, a, b = _config_inputs(cid)
+    out = _fwd(a, b, bs, cfg.trans_b)
+    torch.cuda.synchronize()
+    assert out.shape == (cfg.rows, cfg.dim_out)
+    assert torch.isfinite(out.float()).all()
+    if cid in (1, 4):  # small enough for the oracle on every row
+        want = oracle.round_to(oracle.gmm_oracle_np(a.cpu(), b.cpu(), bs, cfg.trans_b),
+                               oracle.dtype_name(cfg.dtype))
+        ok, nbad, err = oracle.allclose_report(out.float().cpu().numpy(), want,
+                                               oracle.TOLERANCE[oracle.dtype_name(cfg.dtype)])
+        assert ok, (nbad, err)
+    rows, experts, sub_bs = sampled_subproblem(bs.tolist())
+    ridx = torch.as_tensor(rows, device="cuda")
+    check_rows(out[ridx], a[ridx].cpu(), b[experts].cpu(), sub_bs, cfg.trans_b,
+               oracle.dtype_name(cfg.dtype), f"cfg{cid} sampled rows")
+    del a, b, out
+    torch.cuda.empty_cache()
+
+
+def test_config2_checksum_of_checksums():
+    """Size-independent property on the full cfg2 output: row sums of D equal
+    A @ (row sums of B[e]) per expert (linearity), checked at fp32 tolerance."""
+    cfg, bs, a, b = _config_inputs(2)
+    out = _fwd(a, b, bs, False)
+    got = out.float().sum(dim=1)
+    bsum = b.float().sum(dim=2)  # [E, dim]
+    off = 0
+    want = torch.empty_like(got)
+    for e, m in enumerate(bs.tolist()):
+        want[off:off + m] = a[off:off + m].float() @ bsum[e]
+        off += m
+    # bf16 rounding of 14336 outputs per row: error ~ sqrt(N) * ulp/2 * |d|
+    tol = 4.0 * math.sqrt(cfg.dim_out) * 2 ** -8 * out.float().abs().mean().item() + 1e-2
+    assert (got - want).abs().max().item() < tol
