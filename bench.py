@@ -1,0 +1,379 @@
+"""Benchmark of the B200 grouped-GEMM forward (and its expert-parallel layer).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config C] [--impl ours|reference]
+
+One JSON line on rank 0.  A "step" is one grouped-GEMM forward over the
+configuration's full synthetic batch.
+
+* N = 1 (default workload cfg2, the configuration the headline metric is
+  quoted on): ``value`` = FLOPs / step time of ``hopper_gmm_fwd`` with inputs
+  resident in HBM (all inputs are larger than the 126 MB L2, so no flush is
+  needed); ``e2e`` = the same metric through the same public call with the
+  inputs copied in from pinned host memory and D copied back every step.
+* N > 1 (launched by torchrun): expert parallelism -- each rank owns
+  E/N experts and a 1/N share of the tokens; a step is dispatch all-to-all +
+  local grouped GEMM + combine all-to-all (``gmm_b200.ep``).  ``value`` =
+  whole-job FLOPs / max-over-ranks step time; ``tokens_per_s`` = pre-top-k
+  tokens / step time.
+* ``--impl reference``: the reference's own CPU path (its per-expert
+  ``ref_gmm`` loop, restated in ``oracle.ref_gmm_port``) on the host cores,
+  on a bounded row sample of the same workload; rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = ("grouped-GEMM TFLOP/s per B200 (% of tcgen05 peak); "
+          "EP tokens/s at 1/2/4/8 GPUs")
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", type=int, default=None,
+                    help="workload config 1-5 (default: 2 at N=1, 2 with EP at N>1)")
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernel-only", action="store_true",
+                    help="warm-up + timed launches only (no e2e / CPU baseline / clocks): the "
+                         "command profiled with ncu")
+    return ap.parse_args()
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return p, "measured"
+    except (OSError, ValueError):
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+def load_traffic(key):
+    try:
+        with open(os.path.join(ROOT, "profiles", "ncu_traffic.json")) as f:
+            return json.load(f).get(key)
+    except (OSError, ValueError):
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling around the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        if self.index < 0:
+            return self
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "50"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.15)
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.1)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_rate(cfg, a_cpu, b_cpu, bs, budget_s=10.0):
+    """Time the reference's CPU path (ref_gmm restated) on a bounded row sample.
+
+    Returns (TFLOP/s, sample description, cores).  The sample keeps every
+    expert's full B and takes the first r rows of each expert, r grown until
+    one call takes about budget_s / 4 seconds."""
+    import torch
+    import oracle
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    bsl = [int(v) for v in bs]
+    off = [0]
+    for m in bsl:
+        off.append(off[-1] + m)
+
+    def sample(r):
+        sub = [min(m, r) for m in bsl]
+        idx = torch.cat([torch.arange(off[e], off[e] + sub[e]) for e in range(len(bsl)) if sub[e]])
+        return a_cpu[idx], torch.tensor(sub, dtype=torch.int64), sum(sub)
+
+    r = 8
+    while True:
+        a_s, bs_s, rows = sample(r)
+        t0 = time.perf_counter()
+        oracle.ref_gmm_port(a_s, b_cpu, bs_s, cfg.trans_b)
+        dt = time.perf_counter() - t0
+        if dt > budget_s / 4 or r >= max(bsl):
+            break
+        r = min(max(bsl), int(r * max(2.0, (budget_s / 4) / max(dt, 1e-4))))
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while len(times) < 3 or (time.perf_counter() < t_end and len(times) < 50):
+        t0 = time.perf_counter()
+        oracle.ref_gmm_port(a_s, b_cpu, bs_s, cfg.trans_b)
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    flops = 2.0 * rows * cfg.dim * cfg.dim_out
+    desc = (f"oracle.ref_gmm_port (torch CPU {oracle.dtype_name(cfg.dtype)}, per-expert matmul) "
+            f"on the first {min(r, max(bsl))} rows of each expert ({rows} of {cfg.rows} rows, "
+            f"all {len(bsl)} experts' B); median of {len(times)} runs")
+    return flops / med / 1e12, desc, cores
+
+
+def cpu_inputs(cfg, a_dev, b_dev, bs, max_rows_per_expert=None):
+    """CPU copies of the device inputs (the exact bytes the kernel saw)."""
+    return a_dev.cpu(), b_dev.cpu()
+
+
+# ------------------------------------------------------------------------ N = 1
+def run_single(args):
+    import torch
+    import gmm_b200
+    from gmm_b200 import hopper_gmm_fwd
+    from gmm_b200.configs import CONFIGS, batch_sizes_for, make_inputs
+
+    cid = args.config or 2
+    cfg = CONFIGS[cid]
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    bs = batch_sizes_for(cfg)
+    if cid == 1:
+        a, b = [t.to(dev) for t in make_inputs(cfg, "cpu")]
+    else:
+        a, b = make_inputs(cfg, "cuda")
+    flops = cfg.flops()
+    alg_bytes = cfg.algorithmic_bytes(bs)
+    launches_per_step = 3 if cfg.dtype == torch.float32 else 1
+
+    stream = torch.cuda.current_stream()
+    for _ in range(max(3, args.warmup)):
+        hopper_gmm_fwd(a, b, bs, cfg.trans_b)
+    torch.cuda.synchronize()
+    l2_note = "inputs larger than L2 (126 MB)" if alg_bytes > 2 * 126e6 else "L2 flushed between steps"
+    flush = torch.empty(int(256e6), dtype=torch.uint8, device=dev) if alg_bytes <= 2 * 126e6 else None
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    with ClockSampler(-1 if args.kernel_only else 0) as clk:
+        torch.cuda.synchronize()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for i in range(args.steps):
+            if flush is not None:
+                flush.zero_()
+            starts[i].record(stream)
+            hopper_gmm_fwd(a, b, bs, cfg.trans_b)
+            ends[i].record(stream)
+        t1.record(stream)
+        torch.cuda.synchronize()
+    kernel_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    step_ms = statistics.fmean(kernel_ms)
+    if args.kernel_only:
+        print(json.dumps({"config": f"cfg{cid}", "ms_per_step": step_ms,
+                          "value": flops / (step_ms * 1e-3) / 1e12, "unit": "TFLOP/s"}), flush=True)
+        return
+    p50_us = statistics.median(kernel_ms) * 1e3
+    value = flops / (step_ms * 1e-3) / 1e12
+
+    # ---------------- e2e: pinned host buffers, copies inside the timed region
+    a_h = a.cpu().pin_memory()
+    b_h = b.cpu().pin_memory()
+    d_h = torch.empty((cfg.rows, cfg.dim_out), dtype=cfg.dtype).pin_memory()
+    a_d = torch.empty_like(a)
+    b_d = torch.empty_like(b)
+
+    def e2e_step():
+        a_d.copy_(a_h, non_blocking=True)
+        b_d.copy_(b_h, non_blocking=True)
+        d = hopper_gmm_fwd(a_d, b_d, bs, cfg.trans_b)
+        d_h.copy_(d, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    e_steps = max(1, min(args.e2e_steps, args.steps))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / e_steps
+    es = a.element_size()
+    h2d = (a.numel() + b.numel()) * es
+    d2h = cfg.rows * cfg.dim_out * es
+
+    peaks, peak_src = load_peaks()
+    if cfg.dtype == torch.float32 or cid in (3, 4):
+        bound, achieved, peak, unit = "hbm", alg_bytes / (step_ms * 1e-3) / 1e9, peaks["hbm_gbs"], "GB/s"
+    else:
+        bound, achieved, peak, unit = "tensor", value, peaks["bf16_tflops"], "TFLOP/s"
+    traffic = load_traffic(f"cfg{cid}")
+
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 4),
+        "p50_us_per_call": round(p50_us, 2),
+        "tokens_per_s": round(cfg.tokens / (step_ms * 1e-3), 1),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": {torch.bfloat16: "bf16", torch.float16: "fp16", torch.float32: "fp32"}[cfg.dtype],
+        "data": "synthetic (seeded routing -> batch_sizes; A ~ N(0,1), B ~ N(0,1/dim))",
+        "config": {"workload": f"cfg{cid}: {cfg.name}", "experts": cfg.num_experts,
+                   "dim": cfg.dim, "dim_out": cfg.dim_out, "tokens": cfg.tokens,
+                   "top_k": cfg.top_k, "rows": cfg.rows, "trans_b": cfg.trans_b,
+                   "parallelism": "ep1", "l2": l2_note},
+        "e2e": {"value": round(flops / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+                "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": int(h2d),
+                "d2h_bytes_per_step": int(d2h),
+                "path": "pinned host A,B -> device; hopper_gmm_fwd; D -> pinned host"},
+        "gpu_launches": args.steps * launches_per_step,
+        "roofline": {"bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": unit,
+                     "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "peak_source": f"{peak_src} ({'burst' if unit == 'TFLOP/s' else 'copy'})",
+                     "algorithmic": {"flops": flops, "bytes": alg_bytes}},
+        "clocks": clk.summary(),
+    }
+    if not args.no_cpu_baseline:
+        a_c, b_c = cpu_inputs(cfg, a, b, bs)
+        rate, desc, cores = cpu_rate(cfg, a_c, b_c, bs)
+        line["cpu_baseline"] = {"value": round(rate, 4), "unit": "TFLOP/s", "cores": cores,
+                                "kind": "port", "sample": desc}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ reference arm
+def run_reference(args):
+    import torch
+    from gmm_b200.configs import CONFIGS, batch_sizes_for, make_inputs
+    import oracle
+
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cid = args.config or 2
+    cfg = CONFIGS[cid]
+    bs = batch_sizes_for(cfg)
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    # Bounded sample: every expert's full B, the first r rows of each expert,
+    # r sized so one step takes about a second on this host.
+    gen = torch.Generator().manual_seed(cfg.seed)
+    from gmm_b200.configs import b_shape
+    shape = b_shape(cfg)
+    b = torch.empty(*shape, dtype=cfg.dtype)
+    for e in range(shape[0]):
+        b[e] = (torch.randn(*shape[1:], generator=gen) / math.sqrt(cfg.dim)).to(cfg.dtype)
+    bsl = [int(v) for v in bs]
+    r = 4
+    while True:
+        sub = [min(m, r) for m in bsl]
+        a = torch.randn(sum(sub), cfg.dim, generator=gen).to(cfg.dtype)
+        bs_s = torch.tensor(sub, dtype=torch.int64)
+        t0 = time.perf_counter()
+        oracle.ref_gmm_port(a, b, bs_s, cfg.trans_b)
+        dt = time.perf_counter() - t0
+        if dt > 0.5 or r >= max(bsl):
+            break
+        r = min(max(bsl), int(r * max(2.0, 0.8 / max(dt, 1e-4))))
+    for _ in range(max(1, args.warmup)):
+        oracle.ref_gmm_port(a, b, bs_s, cfg.trans_b)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        oracle.ref_gmm_port(a, b, bs_s, cfg.trans_b)
+        times.append(time.perf_counter() - t0)
+        if sum(times) > 120:
+            break
+    step = statistics.fmean(times)
+    rows = sum(sub)
+    value = 2.0 * rows * cfg.dim * cfg.dim_out / step / 1e12
+    desc = (f"reference ref_gmm restated (oracle.ref_gmm_port, torch CPU "
+            f"{oracle.dtype_name(cfg.dtype)}) on the first {min(r, max(bsl))} rows of each expert "
+            f"({rows} of {cfg.rows} rows, full B); {len(times)} timed steps")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "TFLOP/s",
+        "n_gpus": args.gpus, "steps": len(times), "warmup": args.warmup,
+        "ms_per_step": round(step * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": oracle.dtype_name(cfg.dtype), "data": "synthetic",
+        "config": {"workload": f"cfg{cid}: {cfg.name}", "experts": cfg.num_experts, "dim": cfg.dim,
+                   "dim_out": cfg.dim_out, "tokens": cfg.tokens, "top_k": cfg.top_k,
+                   "rows": cfg.rows, "trans_b": cfg.trans_b, "parallelism": "cpu host",
+                   "sampled_rows": rows},
+        "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": cores,
+                         "kind": "port", "sample": desc},
+        "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world > 1 or args.gpus > 1:
+        from gmm_b200 import ep_bench
+        ep_bench.run(args, METRIC, load_peaks, ClockSampler)
+        return
+    run_single(args)
+
+
+if __name__ == "__main__":
+    main()
