@@ -746,3 +746,120 @@ int gmm_sm100_device_error(int* status_out, int clear) {
 }
 
 }  // extern "C"
+
+// ============================================================ allocation-free fp32 entry
+// The scratch of gmm_sm100_forward_f32_noalloc: a fixed device array in this
+// library, so that callers which cannot allocate device memory can still use
+// the fp32 (3xTF32) path.  Host code must not use the symbol's name as a
+// pointer; the device address comes from cudaGetSymbolAddress, once per device.
+namespace gmm_sm100 {
+static __device__ __align__(256) unsigned char g_noalloc_scratch[GMM_SM100_NOALLOC_SCRATCH_BYTES];
+}  // namespace gmm_sm100
+
+namespace {
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on device `dev` (which must be current).
+int noalloc_scratch_address(int dev, void** out) {
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, gmm_sm100::g_noalloc_scratch);
+    if (e != cudaSuccess || !p) return cuda_fail(e, "cudaGetSymbolAddress(noalloc scratch)");
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return GMM_OK;
+}
+
+}  // namespace
+
+extern "C" int gmm_sm100_forward_f32_noalloc(const float* A, const float* B,
+                                             const int64_t* batch_sizes, int64_t num_experts,
+                                             int64_t num_tokens, int64_t dim, int64_t dim_out,
+                                             int trans_b, float* D, void* stream_ptr) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  Plan pl;
+  int rc = make_plan(batch_sizes, num_experts, num_tokens, dim, dim_out, GMM_DTYPE_F32, pl);
+  if (rc != GMM_OK) return rc;
+  const int64_t T = num_tokens, K = dim, N = dim_out, E = num_experts;
+  if (T == 0 || N == 0) return GMM_OK;
+  if (!D) return fail(GMM_ERR_INVALID_ARGUMENT, "D is null");
+  if (!aligned16(D)) return fail(GMM_ERR_ALIGNMENT, "D must be 16-byte aligned");
+  if ((N * 4) % 16 != 0)
+    return fail(GMM_ERR_ALIGNMENT, "dim_out must be a multiple of 4 for fp32, got " + std::to_string(N));
+  const size_t need = pl.split_bytes + pl.table_bytes;
+  if (need > GMM_SM100_NOALLOC_SCRATCH_BYTES)
+    return fail(GMM_ERR_TOO_LARGE, "gmm_sm100_forward_f32_noalloc needs " + std::to_string(need) +
+                                       " bytes of scratch; its fixed scratch holds " +
+                                       std::to_string(GMM_SM100_NOALLOC_SCRATCH_BYTES) +
+                                       " bytes (use gmm_sm100_forward with a workspace)");
+  int dev = 0;
+  cudaError_t ce = cudaGetDevice(&dev);
+  if (ce != cudaSuccess) return cuda_fail(ce, "cudaGetDevice");
+  DeviceInfo* di = nullptr;
+  if ((rc = device_info(dev, &di)) != GMM_OK) return rc;
+  if (K == 0) {
+    ce = cudaMemsetAsync(D, 0, static_cast<size_t>(T) * N * 4, stream);
+    return ce == cudaSuccess ? GMM_OK : cuda_fail(ce, "cudaMemsetAsync");
+  }
+  if (!A || !B) return fail(GMM_ERR_INVALID_ARGUMENT, "A or B is null");
+  if (!aligned16(A) || !aligned16(B)) return fail(GMM_ERR_ALIGNMENT, "A and B must be 16-byte aligned");
+  if ((K * 4) % 16 != 0)
+    return fail(GMM_ERR_ALIGNMENT, "dim must be a multiple of 4 for fp32, got " + std::to_string(K));
+  void* scratch = nullptr;
+  if ((rc = noalloc_scratch_address(dev, &scratch)) != GMM_OK) return rc;
+  uint8_t* ws = static_cast<uint8_t*>(scratch);
+
+  GmmParams prm;
+  std::memset(&prm, 0, sizeof(prm));
+  prm.d = D;
+  prm.ldd = N;
+  prm.num_groups = pl.num_groups;
+  prm.n_tiles = pl.n_tiles;
+  prm.k_blocks = pl.k_blocks;
+  prm.total_tiles = pl.total_tiles;
+  prm.dim_out = static_cast<int>(N);
+  if (pl.table_bytes == 0) {
+    std::memcpy(prm.inline_table, pl.table.data(), pl.table.size() * sizeof(int32_t));
+  } else {
+    uint8_t* tdev = ws + pl.split_bytes;
+    ce = cudaMemcpyAsync(tdev, pl.table.data(), pl.table.size() * sizeof(int32_t), cudaMemcpyHostToDevice, stream);
+    if (ce != cudaSuccess) return cuda_fail(ce, "cudaMemcpyAsync(table)");
+    prm.ext_table = reinterpret_cast<const int32_t*>(tdev);
+  }
+  // Every byte of the scratch that the GEMM reads is rewritten below first.
+  float* a_hi = reinterpret_cast<float*>(ws);
+  float* a_lo = reinterpret_cast<float*>(ws + pl.a_part);
+  float* b_hi = reinterpret_cast<float*>(ws + 2 * pl.a_part);
+  float* b_lo = reinterpret_cast<float*>(ws + 2 * pl.a_part + pl.b_part);
+  const long long n4a = T * K / 4;
+  const int sgrid = static_cast<int>(std::min<long long>((n4a + 255) / 256, 4LL * di->sm_count));
+  split_tf32_kernel<<<std::max(sgrid, 1), 256, 0, stream>>>(
+      reinterpret_cast<const float4*>(A), reinterpret_cast<float4*>(a_hi), reinterpret_cast<float4*>(a_lo), n4a);
+  if (trans_b) {
+    const long long n4b = E * K * N / 4;
+    const int bgrid = static_cast<int>(std::min<long long>((n4b + 255) / 256, 4LL * di->sm_count));
+    split_tf32_kernel<<<std::max(bgrid, 1), 256, 0, stream>>>(
+        reinterpret_cast<const float4*>(B), reinterpret_cast<float4*>(b_hi), reinterpret_cast<float4*>(b_lo), n4b);
+  } else {
+    dim3 tg(static_cast<unsigned>((N + 31) / 32), static_cast<unsigned>((K + 31) / 32), static_cast<unsigned>(E));
+    split_tf32_transpose_kernel<<<tg, dim3(32, 8), 0, stream>>>(B, b_hi, b_lo, static_cast<int>(K), static_cast<int>(N));
+  }
+  ce = cudaGetLastError();
+  if (ce != cudaSuccess) return cuda_fail(ce, "split pre-pass launch");
+  const cuuint64_t uT = T, uK = K, uN = N, uE = E;
+  const cuuint64_t adims[2] = {uK, uT}, astr[1] = {uK * 4};
+  const cuuint32_t abox[2] = {32, 128};
+  const cuuint64_t bdims[3] = {uK, uN, uE}, bstr[2] = {uK * 4, uN * uK * 4};
+  const cuuint32_t bbox[3] = {32, 128, 1};
+  if ((rc = encode(&prm.tmap_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a_hi, adims, astr, abox)) ||
+      (rc = encode(&prm.tmap_a2, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a_lo, adims, astr, abox)) ||
+      (rc = encode(&prm.tmap_b, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, b_hi, bdims, bstr, bbox)) ||
+      (rc = encode(&prm.tmap_b2, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, b_lo, bdims, bstr, bbox)))
+    return rc;
+  const int grid = std::max(1, std::min(pl.total_tiles, di->sm_count));
+  return launch_variant<kKindTf32x3, false>(prm, grid, stream, di, 0);
+}

@@ -88,6 +88,34 @@ int gmm_sm100_forward(const void* A, const void* B, const int64_t* batch_sizes,
  * reference kernel has no device-side error path). */
 int gmm_sm100_device_error(int* status_out, int clear);
 
+/* Size of the fixed scratch area used by gmm_sm100_forward_f32_noalloc. */
+#define GMM_SM100_NOALLOC_SCRATCH_BYTES (8u << 20) /* 8 MiB */
+
+/* fp32 grouped-GEMM forward that allocates no memory at all.  No counterpart
+ * in the reference; it exists for callers that cannot allocate device memory
+ * themselves -- for example a plugin running inside a host engine that owns
+ * every device allocation and its budget, or a latency-critical caller that
+ * cannot afford cudaMalloc / cudaFree, which may synchronise the whole device.
+ *
+ * Same arguments and results as gmm_sm100_forward with dtype GMM_DTYPE_F32
+ * (three TF32 tensor-core products), minus the workspace: the hi/lo TF32
+ * splits of A and B (and the tile table, for more than 1024 non-empty
+ * experts) go to a scratch array of GMM_SM100_NOALLOC_SCRATCH_BYTES compiled
+ * into the library, which every GPU that loads the library keeps until the
+ * process exits.  Problems whose scratch need
+ *   2*num_tokens*dim*4 + 2*num_experts*dim*dim_out*4  (each rounded up to 256 B)
+ * exceeds that size are rejected with GMM_ERR_TOO_LARGE before any GPU work.
+ *
+ * The first call on a device looks up the scratch array's device address
+ * (cudaGetSymbolAddress) with that device current; make that first call
+ * before any stream capture.  All calls share the one scratch array, and its
+ * contents are fully rewritten by each call before they are read: calls whose
+ * GPU work overlaps (different streams, or different host threads, on one
+ * device) race on it and must be serialised by the caller. */
+int gmm_sm100_forward_f32_noalloc(const float* A, const float* B, const int64_t* batch_sizes,
+                                  int64_t num_experts, int64_t num_tokens, int64_t dim,
+                                  int64_t dim_out, int trans_b, float* D, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
