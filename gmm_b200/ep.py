@@ -8,19 +8,26 @@ moves token rows with one exchange step each way:
 1. counts: every rank's host ``batch_sizes`` (rows per global expert) are
    all-gathered over a CPU (gloo) group, so every split size is known on the
    host without a device synchronisation;
-2. dispatch: rank r's rows for expert g go to g's owner, posted as one NCCL
-   point-to-point message per (expert, peer) chunk that lands directly in
-   the owner's expert-major receive buffer (all sources of local expert 0,
-   then of local expert 1, ...);
-3. local grouped GEMM over the E/W local experts (``hopper_gmm_fwd``), one
-   contiguous segment per local expert;
+2. dispatch: rank r's rows for expert g go to g's owner as NCCL
+   point-to-point messages that land directly in the owner's expert-major
+   receive buffer (all sources of local expert 0, then of local expert 1, ...);
+3. local grouped GEMM over the E/W local experts;
 4. combine: each (expert, source) block of the result goes back to its
    source, into the rows the source's A occupied.
 
-Rank r owns experts ``[r*E/W, (r+1)*E/W)``.  The output rows are the input
-rows' results, bit-identical to the single-GPU op on the same rows.  There
-is no CPU fallback: ``local_gemm`` defaults to the CUDA operator; only the
-tests substitute the CPU oracle to check the exchange logic on gloo ranks.
+Pipelining: the owner's expert-major rows are cut into ``chunks`` pieces
+(whole (expert, source-group) blocks, balanced by rows).  All dispatch
+messages are posted first, chunk by chunk; chunk c's GEMM waits only for
+chunk c's rows, and chunk c's combine runs on NCCL's stream while chunk
+c+1's GEMM runs on the compute stream.  Every rank derives every owner's
+chunking from the gathered counts, so both ends of each message agree on
+which batch carries it.
+
+Rank r owns experts ``[r*E/W, (r+1)*E/W)``.  Output rows are bit-identical
+to the single-GPU operator on the same rows.  There is no CPU fallback: the
+local GEMM is the CUDA kernel (through the C ABI, writing in place into a
+reused buffer) unless a test substitutes the CPU oracle to check the
+exchange logic on gloo ranks.
 """
 
 from __future__ import annotations
@@ -31,10 +38,40 @@ import torch
 import torch.distributed as dist
 
 
-def _default_local_gemm(a: torch.Tensor, b: torch.Tensor, batch_sizes: torch.Tensor,
-                        trans_b: bool) -> torch.Tensor:
-    from gmm_b200 import hopper_gmm_fwd
-    return hopper_gmm_fwd(a, b, batch_sizes, trans_b=trans_b)
+class _Chunking:
+    """Every owner's blocks and chunks for one exchange (identical on all ranks)."""
+
+    def __init__(self, all_bs: List[List[int]], world: int, e_local: int, chunks: int):
+        self.W, self.El = world, e_local
+        n_src_groups = max(1, -(-chunks // e_local))  # ceil(chunks / El)
+        n_src_groups = min(n_src_groups, world)
+        bounds = [round(j * world / n_src_groups) for j in range(n_src_groups + 1)]
+        self.src_groups = [(bounds[j], bounds[j + 1]) for j in range(n_src_groups)]
+        self.chunks = chunks
+        # per owner p: list of chunks, each a list of blocks (e, s0, s1, rows)
+        self.owner_chunks = []
+        for p in range(world):
+            blocks = []
+            for e in range(e_local):
+                g = p * e_local + e
+                for (s0, s1) in self.src_groups:
+                    rows = sum(all_bs[s][g] for s in range(s0, s1))
+                    blocks.append((e, s0, s1, rows))
+            total = sum(b[3] for b in blocks)
+            out = [[] for _ in range(chunks)]
+            acc = 0
+            for b in blocks:  # contiguous blocks -> chunk by row-count quantile
+                c = min(chunks - 1, (acc * chunks) // max(total, 1))
+                out[c].append(b)
+                acc += b[3]
+            self.owner_chunks.append(out)
+
+    def chunk_of(self, p: int, e: int, s: int) -> int:
+        for c, blocks in enumerate(self.owner_chunks[p]):
+            for (be, s0, s1, _) in blocks:
+                if be == e and s0 <= s < s1:
+                    return c
+        raise KeyError((p, e, s))
 
 
 class ExpertParallelGmm:
@@ -45,12 +82,13 @@ class ExpertParallelGmm:
         group: process group carrying the token rows (NCCL for GPUs).
         count_group: CPU (gloo) group for the host-side count exchange; created
             from the world if not given.
-        local_gemm: ``f(a, b_local, batch_sizes, trans_b) -> d`` for the local
-            experts; the CUDA operator unless a test substitutes a checker.
+        local_gemm: ``f(a, b_local, batch_sizes, trans_b) -> d`` replacing the CUDA
+            kernel (tests only: checks the exchange logic on CPU ranks).
+        chunks: pipeline depth (GEMM / combine overlap); default 4.
     """
 
     def __init__(self, num_experts: int, group=None, count_group=None,
-                 local_gemm: Optional[Callable] = None):
+                 local_gemm: Optional[Callable] = None, chunks: int = 4):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -62,9 +100,12 @@ class ExpertParallelGmm:
         if count_group is None:
             count_group = group if dist.get_backend(group) == "gloo" else dist.new_group(backend="gloo")
         self.count_group = count_group
-        self.local_gemm = local_gemm or _default_local_gemm
-        self._peer_ranks = [dist.get_global_rank(group, i) if group is not None else i
-                            for i in range(self.world)]
+        self.local_gemm = local_gemm
+        self.chunks = max(1, int(chunks))
+        self._peer = [dist.get_global_rank(group, i) if group is not None else i
+                      for i in range(self.world)]
+        self._x = None
+        self._y = None
 
     # ------------------------------------------------------------------ plan
     def exchange_counts(self, batch_sizes: torch.Tensor) -> torch.Tensor:
@@ -78,27 +119,23 @@ class ExpertParallelGmm:
         dist.all_gather(out, batch_sizes.contiguous(), group=self.count_group)
         return torch.stack(out)
 
-    def plan(self, all_bs: torch.Tensor):
-        """Split sizes and offsets of one exchange, from the gathered counts."""
-        W, El, r = self.world, self.e_local, self.rank
-        bs = all_bs.tolist()
-        mine = [[bs[s][r * El + e] for s in range(W)] for e in range(El)]  # [local e][src]
-        local_bs = [sum(row) for row in mine]
-        # expert-major receive offsets: (e, s)
-        recv_off = []
-        off = 0
-        for e in range(El):
-            row = []
-            for s in range(W):
-                row.append(off)
-                off += mine[e][s]
-            recv_off.append(row)
-        # this rank's own row offsets per global expert (its A / output layout)
-        my_off, o = [], 0
-        for g in range(self.num_experts):
-            my_off.append(o)
-            o += bs[r][g]
-        return mine, local_bs, recv_off, my_off, off
+    def _buffer(self, name, rows, cols, like):
+        buf = getattr(self, name)
+        need = rows * cols
+        if buf is None or buf.numel() < need or buf.dtype != like.dtype or buf.device != like.device:
+            buf = torch.empty(max(need, 1), dtype=like.dtype, device=like.device)
+            setattr(self, name, buf)
+        return buf[:need].view(rows, cols)
+
+    def _gemm_into(self, x, b, bs_list, trans_b, y):
+        if x.shape[0] == 0:
+            return
+        bs = torch.tensor(bs_list, dtype=torch.int64)
+        if self.local_gemm is not None:
+            y.copy_(self.local_gemm(x, b, bs, trans_b))
+            return
+        from gmm_b200 import capi
+        capi.forward(x, b, bs_list, y, trans_b=trans_b)
 
     # --------------------------------------------------------------- forward
     def forward(self, a: torch.Tensor, b_local: torch.Tensor, batch_sizes: torch.Tensor,
@@ -121,65 +158,100 @@ class ExpertParallelGmm:
                              f"A.size(0) ({a.shape[0]})")
         if all_bs is None:
             all_bs = self.exchange_counts(batch_sizes)
-        mine, local_bs, recv_off, my_off, n_recv = self.plan(all_bs)
-        my_bs = all_bs[r].tolist()
+        bs = all_bs.tolist()
+        ch = _Chunking(bs, W, El, self.chunks)
+        C = ch.chunks
         dim = a.shape[1]
         dim_out = b_local.shape[1] if trans_b else b_local.shape[2]
 
-        # ---- dispatch
-        x = torch.empty(n_recv, dim, dtype=a.dtype, device=a.device)
-        ops: List[dist.P2POp] = []
-        for g in range(self.num_experts):  # sends, in global expert order per peer
-            m = my_bs[g]
-            p = g // El
-            if m == 0 or p == r:
-                continue
-            ops.append(dist.P2POp(dist.isend, a[my_off[g]:my_off[g] + m], self._peer_ranks[p],
-                                  self.group))
-        for e in range(El):  # receives, in local expert order per peer
+        # this rank's row offsets per global expert (its A / output layout)
+        my_off, o = [], 0
+        for g in range(self.num_experts):
+            my_off.append(o)
+            o += bs[r][g]
+        # expert-major receive offsets on this rank: (e, s)
+        recv_off, off = [], 0
+        for e in range(El):
+            row = []
             for s in range(W):
-                m = mine[e][s]
-                if m == 0 or s == r:
+                row.append(off)
+                off += bs[s][r * El + e]
+            recv_off.append(row)
+        n_recv = off
+        x = self._buffer("_x", n_recv, dim, a)
+        y = self._buffer("_y", n_recv, dim_out, a)
+        out = torch.empty(a.shape[0], dim_out, dtype=a.dtype, device=a.device)
+
+        # ---- dispatch: all batches posted up front, one per chunk
+        pending = []
+        for c in range(C):
+            ops: List[dist.P2POp] = []
+            for p in range(W):  # sends: my rows for p's chunk-c experts
+                if p == r:
                     continue
-                ops.append(dist.P2POp(dist.irecv, x[recv_off[e][s]:recv_off[e][s] + m],
-                                      self._peer_ranks[s], self.group))
-        for e in range(El):  # own rows: local copy
+                for (e, s0, s1, _) in ch.owner_chunks[p][c]:
+                    g = p * El + e
+                    m = bs[r][g]
+                    if m and s0 <= r < s1:
+                        ops.append(dist.P2POp(dist.isend, a[my_off[g]:my_off[g] + m],
+                                              self._peer[p], self.group))
+            for s in range(W):  # receives: rows from s for my chunk-c blocks
+                if s == r:
+                    continue
+                for (e, s0, s1, _) in ch.owner_chunks[r][c]:
+                    m = bs[s][r * El + e]
+                    if m and s0 <= s < s1:
+                        ops.append(dist.P2POp(dist.irecv, x[recv_off[e][s]:recv_off[e][s] + m],
+                                              self._peer[s], self.group))
+            pending.append(dist.batch_isend_irecv(ops) if ops else [])
+        for e in range(El):  # own rows
             g = r * El + e
-            m = my_bs[g]
+            m = bs[r][g]
             if m:
                 x[recv_off[e][r]:recv_off[e][r] + m].copy_(a[my_off[g]:my_off[g] + m])
-        if ops:
-            for w in dist.batch_isend_irecv(ops):
+
+        # ---- per chunk: GEMM, then combine (overlaps the next chunk's GEMM)
+        combine_works = []
+        for c in range(C):
+            for w in pending[c]:
                 w.wait()
-
-        # ---- local grouped GEMM
-        y = self.local_gemm(x, b_local, torch.tensor(local_bs, dtype=torch.int64), trans_b)
-
-        # ---- combine
-        out = torch.empty(a.shape[0], dim_out, dtype=y.dtype, device=a.device)
-        ops = []
-        for e in range(El):  # sends back, in local expert order per source
-            for s in range(W):
-                m = mine[e][s]
-                if m == 0 or s == r:
+            blocks = ch.owner_chunks[r][c]
+            if blocks:
+                e_first, e_last = blocks[0][0], blocks[-1][0]
+                row0 = recv_off[e_first][blocks[0][1]]
+                per_e = [0] * (e_last - e_first + 1)
+                for (e, s0, s1, rows) in blocks:
+                    per_e[e - e_first] += rows
+                n = sum(per_e)
+                self._gemm_into(x[row0:row0 + n], b_local[e_first:e_last + 1], per_e, trans_b,
+                                y[row0:row0 + n])
+            ops = []
+            for s in range(W):  # sends back: my chunk-c results owned by source s
+                if s == r:
                     continue
-                ops.append(dist.P2POp(dist.isend, y[recv_off[e][s]:recv_off[e][s] + m],
-                                      self._peer_ranks[s], self.group))
-        for g in range(self.num_experts):  # receives, in global expert order per owner
-            m = my_bs[g]
-            p = g // El
-            if m == 0 or p == r:
-                continue
-            ops.append(dist.P2POp(dist.irecv, out[my_off[g]:my_off[g] + m], self._peer_ranks[p],
-                                  self.group))
-        for e in range(El):
-            g = r * El + e
-            m = my_bs[g]
-            if m:
-                out[my_off[g]:my_off[g] + m].copy_(y[recv_off[e][r]:recv_off[e][r] + m])
-        if ops:
-            for w in dist.batch_isend_irecv(ops):
-                w.wait()
+                for (e, s0, s1, _) in blocks:
+                    m = bs[s][r * El + e]
+                    if m and s0 <= s < s1:
+                        ops.append(dist.P2POp(dist.isend, y[recv_off[e][s]:recv_off[e][s] + m],
+                                              self._peer[s], self.group))
+            for p in range(W):  # receives: my rows computed in p's chunk c
+                if p == r:
+                    continue
+                for (e, s0, s1, _) in ch.owner_chunks[p][c]:
+                    g = p * El + e
+                    m = bs[r][g]
+                    if m and s0 <= r < s1:
+                        ops.append(dist.P2POp(dist.irecv, out[my_off[g]:my_off[g] + m],
+                                              self._peer[p], self.group))
+            for (e, s0, s1, _) in blocks:  # own rows back
+                g = r * El + e
+                m = bs[r][g]
+                if m and s0 <= r < s1:
+                    out[my_off[g]:my_off[g] + m].copy_(y[recv_off[e][r]:recv_off[e][r] + m])
+            if ops:
+                combine_works.extend(dist.batch_isend_irecv(ops))
+        for w in combine_works:
+            w.wait()
         return out
 
     __call__ = forward

@@ -57,6 +57,9 @@ def run(args, metric, load_peaks, clock_sampler):
     from gmm_b200.configs import CONFIGS
     from gmm_b200.ep import ExpertParallelGmm
 
+    # NCCL keeps P2P tensors alive until wait() instead of recording them on its
+    # stream, so the allocator can reuse them at once on the compute stream.
+    os.environ.setdefault("TORCH_NCCL_AVOID_RECORD_STREAMS", "1")
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

@@ -48,7 +48,7 @@ def _rank_inputs(rank, E, dim, dim_out, trans_b, skew):
     return a, b_full, bs
 
 
-def _ep_worker(rank, world, port, E, trans_b, skew):
+def _ep_worker(rank, world, port, E, trans_b, skew, chunks):
     import sys
     sys.path.insert(0, ROOT)
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
@@ -59,7 +59,7 @@ def _ep_worker(rank, world, port, E, trans_b, skew):
         dim, dim_out = 24, 40
         a, b_full, bs = _rank_inputs(rank, E, dim, dim_out, trans_b, skew)
         El = E // world
-        ep = ExpertParallelGmm(E, local_gemm=_oracle_local_gemm)
+        ep = ExpertParallelGmm(E, local_gemm=_oracle_local_gemm, chunks=chunks)
         try:
             ExpertParallelGmm(world * E + 1, local_gemm=_oracle_local_gemm)
             raise AssertionError("indivisible expert count accepted")
@@ -76,10 +76,13 @@ def _ep_worker(rank, world, port, E, trans_b, skew):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,E,trans_b,skew", [(2, 8, False, False), (2, 6, True, True),
-                                                  (4, 8, False, True), (3, 3, True, False)])
-def test_ep_matches_oracle_on_gloo_ranks(world, E, trans_b, skew):
-    mp.spawn(_ep_worker, args=(world, _free_port(), E, trans_b, skew), nprocs=world, join=True)
+@pytest.mark.parametrize("world,E,trans_b,skew,chunks", [
+    (2, 8, False, False, 4), (2, 6, True, True, 4), (4, 8, False, True, 4), (3, 3, True, False, 4),
+    (2, 8, False, True, 1), (4, 8, True, True, 7), (4, 4, False, False, 3)])
+def test_ep_matches_oracle_on_gloo_ranks(world, E, trans_b, skew, chunks):
+    """Chunked pipelines with more or fewer chunks than local experts, skewed loads."""
+    mp.spawn(_ep_worker, args=(world, _free_port(), E, trans_b, skew, chunks), nprocs=world,
+             join=True)
 
 
 def _dropout_worker(rank, world, port, outdir):
