@@ -1,0 +1,249 @@
+// gmm_pair_kernel.cuh -- the CTA-pair (cta_group::2) variant of the persistent
+// grouped-GEMM kernel, for groups with many rows (prefill-sized experts).
+//
+// A cluster of two CTAs on neighbouring SMs computes one 256 x 256 output tile:
+//   * CTA r (r = 0 leader, 1 peer) TMA-loads A rows [row0 + 128 r, +128) and
+//     the B column half [n0 + 128 r, +128) into its own shared memory, in a
+//     6-stage ring of 32 KB per CTA (16 KB A + 16 KB B, 128-byte swizzle);
+//     both CTAs' loads complete on the leader's stage barrier, for which the
+//     leader alone posts the expected byte count.  No load is multicast.
+//   * one thread of the leader issues tcgen05.mma.cta_group::2 M=256 N=256
+//     K=16, reading both CTAs' shared memory; each CTA's TMEM receives its own
+//     128 rows x 256 columns (fp32), double-buffered (512 columns).
+//   * the leader's tcgen05.commit (multicast to both CTAs) frees a stage in
+//     both rings and tells both epilogues that an accumulator is ready; the
+//     four epilogue warps of each CTA drain their rows and arrive on the
+//     leader's accumulator-empty barrier (count 8) through the cluster window.
+// Per CTA this moves 32 KB of operands per 64-deep k-block for the same MMA
+// work the single-CTA 128x256 tile needs 48 KB for.
+#pragma once
+
+template <int kKind, bool kBMnMajor>
+struct PairCfg {
+  static_assert(kKind == kKindBf16 || kKind == kKindF16, "pair tiles are 16-bit only");
+  static constexpr int kElem = 2;
+  static constexpr int BM = 256;      // rows per pair tile
+  static constexpr int BM_CTA = 128;  // rows per CTA
+  static constexpr int BN = 256;      // output columns per tile
+  static constexpr int BN_CTA = 128;  // B columns held by each CTA
+  static constexpr int BK = 64;
+  static constexpr int kStages = 6;
+  static constexpr int kUmmaK = 16;
+  static constexpr int kKSteps = BK / kUmmaK;
+  static constexpr int kABytes = BM_CTA * BK * kElem;  // 16 KB
+  static constexpr int kBBytes = BN_CTA * BK * kElem;  // 16 KB
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kTmemCols = 2 * BN;
+  static constexpr uint32_t kIdesc = make_idesc(kKind == kKindBf16 ? 1u : 0u, kBMnMajor, BM, BN);
+  static constexpr int kSmemBytes = kStages * kStageBytes + 256 + 1024;
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+};
+
+// Spin for `ns` nanoseconds (abort path only: lets in-flight copies land).
+__device__ __forceinline__ void spin_ns(unsigned long long ns) {
+  const unsigned long long t0 = global_timer_ns();
+  while (global_timer_ns() - t0 < ns) {
+  }
+}
+
+template <int kKind, bool kBMnMajor>
+__global__ void __launch_bounds__(kThreads, 1) gmm_pair_kernel(const __grid_constant__ GmmParams p) {
+  using C = PairCfg<kKind, kBMnMajor>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t cta = cluster_cta_rank();  // 0 = leader, 1 = peer
+  const bool leader = (cta == 0);
+
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
+  uint64_t* full_bar = bars;                           // both CTAs' TMA -> leader MMA (leader's)
+  uint64_t* empty_bar = bars + C::kStages;             // leader MMA -> each producer
+  uint64_t* tfull_bar = bars + 2 * C::kStages;         // leader MMA -> each epilogue
+  uint64_t* tempty_bar = bars + 2 * C::kStages + 2;    // 8 epilogue warps -> leader MMA
+  uint64_t* drain_bar = bars + 2 * C::kStages + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * C::kStages + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(smem_u32(full_bar + s), 1);
+      mbar_init(smem_u32(empty_bar + s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(tfull_bar + a), 1);
+      mbar_init(smem_u32(tempty_bar + a), 8);
+    }
+    mbar_init(smem_u32(drain_bar), 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&p.tmap_a);
+    prefetch_tmap(&p.tmap_b);
+  }
+  if (warp == 2) {
+    tmem_alloc_pair(smem_u32(tmem_slot), C::kTmemCols);
+    tmem_relinquish_pair();
+  }
+  // Barriers initialised and TMEM allocated in both CTAs before any remote use.
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int32_t* tab = p.ext_table ? p.ext_table : p.inline_table;
+  TableView tv;
+  tv.row_off = tab;
+  tv.tile_off = tab + p.num_groups + 1;
+  tv.expert = tab + 2 * (p.num_groups + 1);
+  const int n_tiles = p.n_tiles;
+  const int k_blocks = p.k_blocks;
+  const int pair = blockIdx.x >> 1;
+  const int num_pairs = gridDim.x >> 1;
+  bool aborted_here = false;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int g = 0;
+      for (int tile = pair; ok && tile < p.total_tiles; tile += num_pairs) {
+        const Tile t = decode_tile<C::BM, C::BN>(tv, n_tiles, tile, g);
+        const int arow = t.row0 + C::BM_CTA * static_cast<int>(cta);
+        const int bcol = t.n0 + C::BN_CTA * static_cast<int>(cta);
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(smem_u32(empty_bar + stage), phase ^ 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb_local = smem_u32(full_bar + stage);
+          if (leader) mbar_arrive_expect_tx(fb_local, 2 * C::kStageBytes);
+          const uint32_t fb = map_shared_to_rank(fb_local, 0);
+          uint8_t* sa = smem + stage * C::kStageBytes;
+          uint8_t* sb = sa + C::kABytes;
+          const int k0 = kb * C::BK;
+          tma_load_2d_pair(smem_u32(sa), &p.tmap_a, fb, k0, arow);
+          if (kBMnMajor) {
+#pragma unroll
+            for (int c = 0; c < C::BN_CTA / 64; ++c)
+              tma_load_3d_pair(smem_u32(sb + c * (C::BK * 128)), &p.tmap_b, fb, bcol + 64 * c, k0,
+                               t.expert);
+          } else {
+            tma_load_3d_pair(smem_u32(sb), &p.tmap_b, fb, k0, bcol, t.expert);
+          }
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) aborted_here = true;
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader only)
+    if (lane == 0 && leader) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int local = 0;
+      for (int tile = pair; ok && tile < p.total_tiles; tile += num_pairs, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(smem_u32(tempty_bar + acc), acc_phase ^ 1, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * C::BN;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(smem_u32(full_bar + stage), phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * C::kStageBytes);
+          const uint32_t sb = sa + C::kABytes;
+#pragma unroll
+          for (int ks = 0; ks < C::kKSteps; ++ks) {
+            const uint64_t adesc = make_sw128_desc(sa + ks * 32, 16, 1024);
+            const uint64_t bdesc = kBMnMajor
+                                       ? make_sw128_desc(sb + ks * C::kUmmaK * 128, C::BK * 128, 1024)
+                                       : make_sw128_desc(sb + ks * 32, 16, 1024);
+            mma_f16_pair(d_tmem, adesc, bdesc, C::kIdesc, (kb | ks) != 0 ? 1u : 0u);
+          }
+          mma_commit_pair_mc(smem_u32(empty_bar + stage), 0x3);
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit_pair_mc(smem_u32(tfull_bar + acc), 0x3);
+      }
+      mma_commit_pair(smem_u32(drain_bar));
+      mbar_wait_drain(smem_u32(drain_bar), 0);
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    using OutT = typename std::conditional<kKind == kKindBf16, __nv_bfloat16, __half>::type;
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const uint32_t tempty_leader0 = map_shared_to_rank(smem_u32(tempty_bar), 0);
+    int g = 0;
+    int local = 0;
+    for (int tile = pair; tile < p.total_tiles; tile += num_pairs, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(smem_u32(tfull_bar + acc), acc_phase, abort_flag)) break;
+      tc_fence_after();
+      const Tile t = decode_tile<C::BM, C::BN>(tv, n_tiles, tile, g);
+      const int rows_cta = t.rows - C::BM_CTA * static_cast<int>(cta);
+      const int row0 = t.row0 + C::BM_CTA * static_cast<int>(cta);
+      if (quarter * 32 < rows_cta) {  // warp-uniform
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * C::BN;
+        const bool row_live = r < rows_cta;
+        OutT* drow = reinterpret_cast<OutT*>(p.d) + static_cast<long long>(row0 + r) * p.ldd;
+#pragma unroll 1
+        for (int c = 0; c < C::BN / 32; ++c) {
+          const int col = t.n0 + c * 32;
+          if (col >= p.dim_out) break;  // warp-uniform
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(taddr + c * 32, v);
+          tmem_wait_ld();
+          if (!row_live) continue;
+          OutT* out = drow + col;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            if (col + q * 8 < p.dim_out) {
+              uint4 pk;
+              pk.x = pack2<OutT>(__uint_as_float(v[8 * q + 0]), __uint_as_float(v[8 * q + 1]));
+              pk.y = pack2<OutT>(__uint_as_float(v[8 * q + 2]), __uint_as_float(v[8 * q + 3]));
+              pk.z = pack2<OutT>(__uint_as_float(v[8 * q + 4]), __uint_as_float(v[8 * q + 5]));
+              pk.w = pack2<OutT>(__uint_as_float(v[8 * q + 6]), __uint_as_float(v[8 * q + 7]));
+              *reinterpret_cast<uint4*>(out + q * 8) = pk;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty_leader0 + acc * 8);
+    }
+  }
+
+  // --------------------------------------------------------------- teardown
+  if (aborted_here || *abort_flag) spin_ns(2000000);  // in-flight copies land before exit
+  tc_fence_before();
+  __syncwarp();
+  __syncthreads();
+  cluster_sync_all();  // no CTA leaves while its peer may still touch its shared memory
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, C::kTmemCols);
+  }
+  if (threadIdx.x == 0 && *abort_flag) atomicCAS(&g_device_error, 0, GMM_ERR_DEVICE_TIMEOUT);
+  __syncwarp();
+  cluster_sync_all();
+}

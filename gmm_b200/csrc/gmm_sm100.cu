@@ -28,6 +28,7 @@
 #include <algorithm>
 #include <atomic>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -425,6 +426,8 @@ __global__ void split_tf32_transpose_kernel(const float* __restrict__ b, float* 
   }
 }
 
+#include "gmm_pair_kernel.cuh"
+
 }  // namespace gmm_sm100
 
 // =====================================================================  host side
@@ -463,6 +466,7 @@ struct DeviceInfo {
   int sm_count = 0;
   int cc_major = 0, cc_minor = 0;
   std::atomic<unsigned> smem_attr_set{0};  // bit per kernel variant
+  int pair_clusters[16] = {};               // resident CTA pairs per pair-kernel variant
 };
 DeviceInfo g_dev[kMaxDevices];
 std::mutex g_dev_mu;
@@ -501,12 +505,13 @@ struct Plan {
 
 int elem_size(int dtype) { return dtype == GMM_DTYPE_F32 ? 4 : 2; }
 
-int make_plan(const int64_t* bs, int64_t E, int64_t T, int64_t K, int64_t N, int dtype, Plan& pl) {
+int make_plan(const int64_t* bs, int64_t E, int64_t T, int64_t K, int64_t N, int dtype, Plan& pl,
+              int64_t tile_rows = 128) {
   if (E < 0 || T < 0 || K < 0 || N < 0) return fail(GMM_ERR_INVALID_ARGUMENT, "negative size");
   if (E > 0 && !bs) return fail(GMM_ERR_INVALID_ARGUMENT, "batch_sizes is null");
   if (dtype != GMM_DTYPE_F32 && dtype != GMM_DTYPE_BF16 && dtype != GMM_DTYPE_F16)
     return fail(GMM_ERR_DTYPE, "Unsupported dtype: only FP32 / BF16 / FP16 are supported");
-  const int64_t BM = 128;
+  const int64_t BM = tile_rows;
   const int64_t BN = dtype == GMM_DTYPE_F32 ? 128 : 256;
   const int64_t BK = dtype == GMM_DTYPE_F32 ? 32 : 64;
   int64_t sum = 0, groups = 0, mtiles = 0;
@@ -583,6 +588,53 @@ int launch_variant(const GmmParams& prm, int grid, cudaStream_t stream, DeviceIn
   return GMM_OK;
 }
 
+// Launch the CTA-pair kernel: clusters of 2 CTAs, as many pairs as can be
+// resident at once (capped by the tile count).
+template <int kKind, bool kMn>
+int launch_pair(const GmmParams& prm, int total_tiles, cudaStream_t stream, DeviceInfo* di, int bit) {
+  using C = PairCfg<kKind, kMn>;
+  auto kern = gmm_pair_kernel<kKind, kMn>;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (!(di->smem_attr_set.load() & (1u << bit))) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(pair)");
+    cfg.gridDim = dim3(2 * std::max(1, di->sm_count / 2), 1, 1);
+    int clusters = 0;
+    e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
+    if (e != cudaSuccess || clusters <= 0) clusters = di->sm_count / 2;
+    di->pair_clusters[bit] = clusters;
+    di->smem_attr_set.fetch_or(1u << bit);
+  }
+  const int pairs = std::max(1, std::min(total_tiles, di->pair_clusters[bit]));
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, prm);
+  if (e != cudaSuccess) return cuda_fail(e, "gmm pair kernel launch");
+  return GMM_OK;
+}
+
+// Tile rows for a 16-bit problem: 256-row CTA-pair tiles when the non-empty
+// experts average at least 384 rows, else 128-row single-CTA tiles.
+// GMM_SM100_TILE=128 or =256 forces one of them (tests and benchmarks).
+int64_t choose_tile_rows(const int64_t* bs, int64_t E, int64_t T, int dtype) {
+  if (dtype == GMM_DTYPE_F32) return 128;
+  const char* force = std::getenv("GMM_SM100_TILE");
+  if (force && std::strcmp(force, "128") == 0) return 128;
+  if (force && std::strcmp(force, "256") == 0) return 256;
+  int64_t groups = 0;
+  for (int64_t e = 0; e < E; ++e) groups += bs[e] > 0;
+  return (groups > 0 && T >= 384 * groups) ? 256 : 128;
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace
@@ -627,6 +679,10 @@ int gmm_sm100_forward(const void* A, const void* B, const int64_t* batch_sizes, 
   Plan pl;
   int rc = make_plan(batch_sizes, num_experts, num_tokens, dim, dim_out, dtype, pl);
   if (rc != GMM_OK) return rc;
+  const int64_t tile_rows = choose_tile_rows(batch_sizes, num_experts, num_tokens, dtype);
+  if (tile_rows != 128 &&
+      (rc = make_plan(batch_sizes, num_experts, num_tokens, dim, dim_out, dtype, pl, tile_rows)) != GMM_OK)
+    return rc;
   const int64_t T = num_tokens, K = dim, N = dim_out, E = num_experts;
   if (T == 0 || N == 0) return GMM_OK;  // nothing to write
   if (!D) return fail(GMM_ERR_INVALID_ARGUMENT, "D is null");
@@ -712,9 +768,9 @@ int gmm_sm100_forward(const void* A, const void* B, const int64_t* batch_sizes, 
     const cuuint64_t adims[2] = {uK, uT}, astr[1] = {uK * 2};
     const cuuint32_t abox[2] = {64, 128};
     if ((rc = encode(&prm.tmap_a, tt, 2, A, adims, astr, abox))) return rc;
-    if (trans_b) {  // B[e] is [N, K], K contiguous
+    if (trans_b) {  // B[e] is [N, K], K contiguous; a CTA of a pair holds half the tile's columns
       const cuuint64_t bdims[3] = {uK, uN, uE}, bstr[2] = {uK * 2, uN * uK * 2};
-      const cuuint32_t bbox[3] = {64, 256, 1};
+      const cuuint32_t bbox[3] = {64, tile_rows == 256 ? 128u : 256u, 1};
       if ((rc = encode(&prm.tmap_b, tt, 3, B, bdims, bstr, bbox))) return rc;
     } else {  // B[e] is [K, N], N contiguous
       const cuuint64_t bdims[3] = {uN, uK, uE}, bstr[2] = {uN * 2, uK * uN * 2};
@@ -725,6 +781,13 @@ int gmm_sm100_forward(const void* A, const void* B, const int64_t* batch_sizes, 
 
   const int grid = std::max(1, std::min(pl.total_tiles, di->sm_count));
   if (dtype == GMM_DTYPE_F32) return launch_variant<kKindTf32x3, false>(prm, grid, stream, di, 0);
+  if (tile_rows == 256) {
+    if (dtype == GMM_DTYPE_BF16)
+      return trans_b ? launch_pair<kKindBf16, false>(prm, pl.total_tiles, stream, di, 5)
+                     : launch_pair<kKindBf16, true>(prm, pl.total_tiles, stream, di, 6);
+    return trans_b ? launch_pair<kKindF16, false>(prm, pl.total_tiles, stream, di, 7)
+                   : launch_pair<kKindF16, true>(prm, pl.total_tiles, stream, di, 8);
+  }
   if (dtype == GMM_DTYPE_BF16)
     return trans_b ? launch_variant<kKindBf16, false>(prm, grid, stream, di, 1)
                    : launch_variant<kKindBf16, true>(prm, grid, stream, di, 2);

@@ -88,11 +88,13 @@ def run(args, metric, load_peaks, clock_sampler):
         for _ in range(max(3, args.warmup)):
             ep(a, b_local, bs, cfg.trans_b)
         torch.cuda.synchronize()
-        dist.barrier()
         stream = torch.cuda.current_stream()
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
         with clock_sampler(local_rank if rank == 0 else -1) as clk:
+            # all ranks start the timed region together (the sampler start-up
+            # on rank 0 must not count as a peer wait on the other ranks)
+            dist.barrier()
             torch.cuda.synchronize()
             t0.record(stream)
             for _ in range(args.steps):
@@ -119,6 +121,7 @@ def run(args, metric, load_peaks, clock_sampler):
         e2e_step()
         torch.cuda.synchronize()
         dist.barrier()
+        torch.cuda.synchronize()
         e_steps = max(1, min(args.e2e_steps, args.steps))
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)

@@ -33,13 +33,20 @@ def _device():
     assert capi.device_error(clear=True) == 0, "a kernel recorded a device-side timeout"
 
 
+@pytest.fixture(params=["128", "256"])
+def tile(request, monkeypatch):
+    """Run a test with the single-CTA (128-row) or the CTA-pair (256-row) kernel forced."""
+    monkeypatch.setenv("GMM_SM100_TILE", request.param)
+    return request.param
+
+
 def _fwd(a, b, bs, trans_b):
     from gmm_b200 import hopper_gmm_fwd
     return hopper_gmm_fwd(a, b, bs, trans_b=trans_b)
 
 
 @pytest.mark.parametrize("case", CASES, ids=[c["name"] for c in CASES])
-def test_golden_case(case):
+def test_golden_case(case, tile):
     a, b, bs = make_case_inputs(case)
     out = _fwd(a.cuda(), b.cuda(), bs, case["trans_b"])
     torch.cuda.synchronize()
@@ -59,7 +66,7 @@ def test_golden_case(case):
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 @pytest.mark.parametrize("trans_b", [False, True])
-def test_placement_is_exact(dtype, trans_b):
+def test_placement_is_exact(dtype, trans_b, tile):
     """B[e] = (e+1) * I: every output row must be exactly (e+1) * its input row."""
     bs = [5, 0, 300, 1, 129, 0, 128, 17, 0, 64]
     dim = 256
@@ -75,7 +82,7 @@ def test_placement_is_exact(dtype, trans_b):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
-def test_canary_rows_untouched(dtype):
+def test_canary_rows_untouched(dtype, tile):
     """Drive the C ABI into the middle of a NaN-filled buffer: nothing outside D is written."""
     from gmm_b200 import capi
     bs = [3, 0, 200, 0, 70]
@@ -106,7 +113,7 @@ def test_more_groups_than_inline_table():
     assert ok, (nbad, err)
 
 
-def test_degenerate_sizes():
+def test_degenerate_sizes(tile):
     dev = "cuda"
     # all experts empty -> T = 0
     out = _fwd(torch.empty(0, 64, device=dev, dtype=torch.bfloat16),
@@ -143,7 +150,7 @@ def test_reference_error_messages():
         _fwd(torch.randn(64, 10, device=dev).bfloat16().t(), b, torch.tensor([4, 6]), False)
 
 
-def test_deterministic_and_stream_ordered():
+def test_deterministic_and_stream_ordered(tile):
     a = torch.randn(3000, 512, device="cuda").bfloat16()
     b = (torch.randn(4, 512, 768, device="cuda") / 16).bfloat16()
     bs = torch.tensor([1000, 0, 1500, 500])
@@ -170,7 +177,7 @@ def _config_inputs(cid):
 
 
 @pytest.mark.parametrize("cid", [1, 2, 3, 4, 5])
-def test_config_parity(cid):
+def test_config_parity(cid, tile):
     cfg, bs, a, b = _config_inputs(cid)
     out = _fwd(a, b, bs, cfg.trans_b)
     torch.cuda.synchronize()
