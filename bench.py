@@ -284,6 +284,9 @@ def run_single(args):
         "roofline": {"bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": unit,
                      "frac": round(achieved / peak, 4), "traffic": traffic,
                      "peak_source": f"{peak_src} ({'burst' if unit == 'TFLOP/s' else 'copy'})",
+                     **({"peak_sustained": peaks.get("bf16_tflops_sustained"),
+                         "frac_sustained": round(achieved / peaks["bf16_tflops_sustained"], 4)}
+                        if unit == "TFLOP/s" and peaks.get("bf16_tflops_sustained") else {}),
                      "algorithmic": {"flops": flops, "bytes": alg_bytes}},
         "clocks": clk.summary(),
     }
