@@ -49,6 +49,9 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--max-experts", type=int, default=None,
+                    help="keep only the first K experts (and their rows): a smaller case of the "
+                         "same workload for ncu captures")
     ap.add_argument("--kernel-only", action="store_true",
                     help="warm-up + timed launches only (no e2e / CPU baseline / clocks): the "
                          "command profiled with ncu")
@@ -190,6 +193,10 @@ def run_single(args):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     bs = batch_sizes_for(cfg)
+    if args.max_experts:
+        import dataclasses
+        bs = bs[:args.max_experts].clone()
+        cfg = dataclasses.replace(cfg, num_experts=len(bs), tokens=int(bs.sum()), top_k=1)
     if cid == 1:
         a, b = [t.to(dev) for t in make_inputs(cfg, "cpu")]
     else:
