@@ -29,6 +29,17 @@ _SIGNATURES = {
                                          ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
                                          ctypes.c_void_p]),
     "gmm_sm100_device_error": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int), ctypes.c_int]),
+    "gmm_sm100_ep_gather": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                           ctypes.c_void_p, ctypes.c_int64, ctypes.c_int,
+                                           ctypes.c_int64, ctypes.c_void_p]),
+    "gmm_sm100_forward_ep": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                            ctypes.c_void_p, ctypes.c_int64, ctypes.c_int,
+                                            ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                                            ctypes.c_int64, ctypes.c_int, ctypes.c_int,
+                                            ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    "gmm_sm100_ep_workspace_size": (ctypes.c_size_t, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int,
+                                                      ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                                      ctypes.c_int]),
     "gmm_sm100_forward_f32_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p,
                                                      ctypes.c_void_p, ctypes.c_int64,
                                                      ctypes.c_int64, ctypes.c_int64,
@@ -101,3 +112,39 @@ def device_error(clear=True) -> int:
     v = ctypes.c_int(0)
     _check(load().gmm_sm100_device_error(ctypes.byref(v), int(bool(clear))))
     return v.value
+
+
+def _i64(values):
+    import numpy as np
+    return np.ascontiguousarray(np.asarray(values, dtype=np.int64).reshape(-1))
+
+
+def _ptrs(values):
+    return (ctypes.c_void_p * len(values))(*[int(v) for v in values])
+
+
+def ep_gather(x, src_ptrs, counts, src_rows, num_local_experts, row_bytes, stream=None):
+    """Pull the (expert, source) row chunks into ``x`` (see ``gmm_sm100_ep_gather``)."""
+    import torch
+    c, r = _i64(counts), _i64(src_rows)
+    s = torch.cuda.current_stream(x.device).cuda_stream if stream is None else stream
+    _check(load().gmm_sm100_ep_gather(x.data_ptr(), _ptrs(src_ptrs), c.ctypes.data, r.ctypes.data,
+                                      num_local_experts, len(src_ptrs), row_bytes, s))
+
+
+def forward_ep(x, b, counts, dst_rows, num_local_experts, out_ptrs, trans_b=False, stream=None):
+    """Local grouped GEMM whose epilogue writes each row back to its source rank."""
+    import torch
+    c, d = _i64(counts), _i64(dst_rows)
+    W = len(out_ptrs)
+    dtype = dtype_code(x.dtype)
+    dim = x.shape[1]
+    dim_out = b.shape[1] if trans_b else b.shape[2]
+    lib = load()
+    need = int(lib.gmm_sm100_ep_workspace_size(c.ctypes.data, num_local_experts, W, x.shape[0], dim,
+                                               dim_out, dtype))
+    ws = torch.empty(need, dtype=torch.uint8, device=x.device) if need else None
+    s = torch.cuda.current_stream(x.device).cuda_stream if stream is None else stream
+    _check(lib.gmm_sm100_forward_ep(x.data_ptr(), b.data_ptr(), c.ctypes.data, d.ctypes.data,
+                                    num_local_experts, W, _ptrs(out_ptrs), x.shape[0], dim, dim_out,
+                                    dtype, int(bool(trans_b)), ws.data_ptr() if need else None, need, s))

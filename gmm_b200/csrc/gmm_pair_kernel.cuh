@@ -94,11 +94,7 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_pair_kernel(const __grid_cons
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int32_t* tab = p.ext_table ? p.ext_table : p.inline_table;
-  TableView tv;
-  tv.row_off = tab;
-  tv.tile_off = tab + p.num_groups + 1;
-  tv.expert = tab + 2 * (p.num_groups + 1);
+  const TableView tv = make_table_view(p);
   const int n_tiles = p.n_tiles;
   const int k_blocks = p.k_blocks;
   const int pair = blockIdx.x >> 1;
@@ -204,7 +200,7 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_pair_kernel(const __grid_cons
       if (quarter * 32 < rows_cta) {  // warp-uniform
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * C::BN;
         const bool row_live = r < rows_cta;
-        OutT* drow = reinterpret_cast<OutT*>(p.d) + static_cast<long long>(row0 + r) * p.ldd;
+        OutT* drow = row_live ? out_row<OutT>(p, tv, g, row0 + r) : nullptr;
 #pragma unroll 1
         for (int c = 0; c < C::BN / 32; ++c) {
           const int col = t.n0 + c * 32;
@@ -231,6 +227,7 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_pair_kernel(const __grid_cons
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader0 + acc * 8);
     }
+    if (p.remote) __threadfence_system();  // peer stores performed before the kernel ends
   }
 
   // --------------------------------------------------------------- teardown

@@ -43,6 +43,8 @@ namespace gmm_sm100 {
 __device__ int g_device_error = 0;
 
 constexpr int kInlineGroups = 1024;  // groups whose table travels in the kernel parameters
+constexpr int kInlineTableInts = 3 * kInlineGroups + 2;
+constexpr int kMaxPeers = 8;         // expert-parallel ranks a kernel can address
 constexpr int kMBlock = 16;          // m-tiles per raster block (L2 reuse of B columns)
 constexpr int kThreads = 256;        // 8 warps: TMA, MMA, TMEM alloc, idle, 4x epilogue
 
@@ -59,13 +61,18 @@ struct __align__(64) GmmParams {
   int k_blocks;
   int total_tiles;
   int dim_out;
+  int remote;  // 1: output rows go to the ranks they came from (expert-parallel combine)
+  int world;   // ranks addressed through d_peer (remote mode)
   int pad_;
+  void* d_peer[kMaxPeers];  // each rank's output buffer (remote mode)
   // Table of the non-empty groups, laid out as
-  //   row_off[G+1] | tile_off[G+1] | expert[G]
+  //   row_off[G+1] | tile_off[G+1] | expert[G] [| src_off[G][W+1] | dst_row[G][W]]
   // row_off: first row of group g in A/D (row_off[G] = T);
-  // tile_off: prefix sum of m-tiles (ceil(m_g / 128));
-  // expert: index of the expert (B slice) of group g.
-  int32_t inline_table[3 * kInlineGroups + 2];
+  // tile_off: prefix sum of m-tiles (ceil(m_g / tile rows));
+  // expert: index of the expert (B slice) of group g;
+  // remote mode only -- src_off: where each source rank's rows start inside
+  // group g; dst_row: the row on that source where they go back to.
+  int32_t inline_table[kInlineTableInts];
 };
 
 enum Kind : int { kKindTf32x3 = 0, kKindBf16 = 1, kKindF16 = 2 };
@@ -98,7 +105,33 @@ struct TableView {
   const int32_t* row_off;
   const int32_t* tile_off;
   const int32_t* expert;
+  const int32_t* src_off;  // remote mode
+  const int32_t* dst_row;  // remote mode
 };
+
+__device__ __forceinline__ TableView make_table_view(const GmmParams& p) {
+  const int32_t* tab = p.ext_table ? p.ext_table : p.inline_table;
+  TableView tv;
+  tv.row_off = tab;
+  tv.tile_off = tab + p.num_groups + 1;
+  tv.expert = tab + 2 * (p.num_groups + 1);
+  tv.src_off = tv.expert + p.num_groups;
+  tv.dst_row = tv.src_off + p.num_groups * (p.world + 1);
+  return tv;
+}
+
+// Where output row `row` (a row of A, inside group g) is stored: D itself, or
+// in remote mode the output buffer of the rank the row came from.
+template <typename T>
+__device__ __forceinline__ T* out_row(const GmmParams& p, const TableView& tv, int g, int row) {
+  if (!p.remote) return reinterpret_cast<T*>(p.d) + static_cast<long long>(row) * p.ldd;
+  const int grow = row - tv.row_off[g];
+  const int32_t* so = tv.src_off + g * (p.world + 1);
+  int s = 0;
+  while (s + 1 < p.world && grow >= so[s + 1]) ++s;
+  const int32_t* dr = tv.dst_row + g * p.world;
+  return reinterpret_cast<T*>(p.d_peer[s]) + static_cast<long long>(dr[s] + grow - so[s]) * p.ldd;
+}
 
 struct Tile {
   int row0;    // first row of the tile in A / D
@@ -200,11 +233,7 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_persistent_kernel(const __gri
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int32_t* tab = p.ext_table ? p.ext_table : p.inline_table;
-  TableView tv;
-  tv.row_off = tab;
-  tv.tile_off = tab + p.num_groups + 1;
-  tv.expert = tab + 2 * (p.num_groups + 1);
+  const TableView tv = make_table_view(p);
   const int n_tiles = p.n_tiles;
   const int k_blocks = p.k_blocks;
 
@@ -324,7 +353,9 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_persistent_kernel(const __gri
       if (quarter * 32 < t.rows) {  // warp-uniform: some row of this quarter is live
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * C::BN;
         const bool row_live = r < t.rows;
-        const long long drow = static_cast<long long>(t.row0 + r) * p.ldd;
+        using RowT = typename std::conditional<C::kTf32, float,
+            typename std::conditional<kKind == kKindBf16, __nv_bfloat16, __half>::type>::type;
+        RowT* drow = row_live ? out_row<RowT>(p, tv, g, t.row0 + r) : nullptr;
 #pragma unroll 1
         for (int c = 0; c < C::BN / 32; ++c) {
           const int col = t.n0 + c * 32;
@@ -334,7 +365,7 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_persistent_kernel(const __gri
           tmem_wait_ld();
           if (!row_live) continue;
           if (C::kTf32) {
-            float* out = reinterpret_cast<float*>(p.d) + drow + col;
+            float* out = reinterpret_cast<float*>(drow) + col;
 #pragma unroll
             for (int q = 0; q < 8; ++q) {
               if (col + q * 4 < p.dim_out) {
@@ -344,7 +375,7 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_persistent_kernel(const __gri
             }
           } else {
             using OutT = typename std::conditional<kKind == kKindBf16, __nv_bfloat16, __half>::type;
-            OutT* out = reinterpret_cast<OutT*>(p.d) + drow + col;
+            OutT* out = reinterpret_cast<OutT*>(drow) + col;
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
               if (col + q * 8 < p.dim_out) {
@@ -363,6 +394,7 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_persistent_kernel(const __gri
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(tempty_bar + acc));
     }
+    if (p.remote) __threadfence_system();  // peer stores performed before the kernel ends
   }
 
   tc_fence_before();
@@ -423,6 +455,47 @@ __global__ void split_tf32_transpose_kernel(const float* __restrict__ b, float* 
       hi[o] = h;
       lo[o] = l;
     }
+  }
+}
+
+// ------------------------------------------------------------ expert-parallel dispatch
+constexpr int kMaxGatherChunks = 2048;
+
+struct GatherParams {
+  const char* src[kMaxPeers];  // each rank's token rows (peer-accessible)
+  char* x;                     // this rank's expert-major receive buffer
+  long long row_bytes;
+  int n_chunks;
+  int total_rows;
+  int chunk_dst[kMaxGatherChunks + 1];  // first row of each chunk in x (prefix sums)
+  int chunk_rank[kMaxGatherChunks];     // source rank of the chunk
+  int chunk_row[kMaxGatherChunks];      // first row of the chunk in the source
+};
+
+// One warp per row: pull each row of x from the rank it lives on over
+// NVLink (plain peer loads, 16 bytes per lane, 4 in flight per lane).
+__global__ void __launch_bounds__(256) ep_gather_kernel(const __grid_constant__ GatherParams p) {
+  const int lane = threadIdx.x & 31;
+  const int warps = (gridDim.x * blockDim.x) >> 5;
+  for (int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < p.total_rows; row += warps) {
+    int lo = 0, hi = p.n_chunks - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (p.chunk_dst[mid] <= row) lo = mid; else hi = mid - 1;
+    }
+    const uint4* src = reinterpret_cast<const uint4*>(
+        p.src[p.chunk_rank[lo]] + static_cast<long long>(p.chunk_row[lo] + row - p.chunk_dst[lo]) * p.row_bytes);
+    uint4* dst = reinterpret_cast<uint4*>(p.x + static_cast<long long>(row) * p.row_bytes);
+    const int n16 = static_cast<int>(p.row_bytes >> 4);
+    int i = lane;
+    for (; i + 96 < n16; i += 128) {
+      const uint4 v0 = src[i], v1 = src[i + 32], v2 = src[i + 64], v3 = src[i + 96];
+      dst[i] = v0;
+      dst[i + 32] = v1;
+      dst[i + 64] = v2;
+      dst[i + 96] = v3;
+    }
+    for (; i < n16; i += 32) dst[i] = src[i];
   }
 }
 
@@ -637,44 +710,44 @@ int64_t choose_tile_rows(const int64_t* bs, int64_t E, int64_t T, int dtype) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-}  // namespace
+// Expert-parallel routing of a local grouped GEMM: rows of local expert e
+// arrive from source ranks s = 0..world-1 in order (counts[e*world + s] rows
+// each) and their results go back to row dst_rows[e*world + s] of rank s's
+// output buffer out_peers[s].
+struct EpRoute {
+  int world;
+  void* const* out_peers;
+  const int64_t* counts;
+  const int64_t* dst_rows;
+};
 
-extern "C" {
-
-const char* gmm_sm100_errstr(int status) {
-  switch (status) {
-    case GMM_OK: return "ok";
-    case GMM_ERR_INVALID_ARGUMENT: return "invalid argument";
-    case GMM_ERR_BATCH_SUM: return "sum of batch_sizes does not match the number of rows";
-    case GMM_ERR_DTYPE: return "unsupported dtype";
-    case GMM_ERR_ALIGNMENT: return "misaligned pointer or row pitch";
-    case GMM_ERR_ARCH: return "unsupported GPU architecture (needs sm_100)";
-    case GMM_ERR_CUDA: return "CUDA error";
-    case GMM_ERR_WORKSPACE: return "workspace too small";
-    case GMM_ERR_TOO_LARGE: return "problem too large";
-    case GMM_ERR_DEVICE_TIMEOUT: return "device-side wait timed out";
-    default: return "unknown status";
+// Append src_off[G][W+1] | dst_row[G][W] for the non-empty groups and decide
+// whether the table still fits in the kernel parameters.
+bool append_ep_table(Plan& pl, const int64_t* local_bs, int64_t E, const EpRoute& ep) {
+  const int W = ep.world;
+  std::vector<int32_t> src, dst;
+  for (int64_t e = 0; e < E; ++e) {
+    if (local_bs[e] <= 0) continue;
+    int64_t acc = 0;
+    for (int s = 0; s < W; ++s) {
+      src.push_back(static_cast<int32_t>(acc));
+      acc += ep.counts[e * W + s];
+      if (ep.dst_rows[e * W + s] < 0 || ep.dst_rows[e * W + s] > INT32_MAX) return false;
+      dst.push_back(static_cast<int32_t>(ep.dst_rows[e * W + s]));
+    }
+    src.push_back(static_cast<int32_t>(acc));
   }
+  pl.table.insert(pl.table.end(), src.begin(), src.end());
+  pl.table.insert(pl.table.end(), dst.begin(), dst.end());
+  pl.table_bytes = pl.table.size() > static_cast<size_t>(kInlineTableInts)
+                       ? round_up(pl.table.size() * sizeof(int32_t), 256)
+                       : 0;
+  return true;
 }
 
-const char* gmm_sm100_last_error(void) { return t_last_error.c_str(); }
-
-int gmm_sm100_check_device(int device) {
-  DeviceInfo* di = nullptr;
-  return device_info(device, &di);
-}
-
-size_t gmm_sm100_workspace_size(const int64_t* batch_sizes, int64_t num_experts, int64_t num_tokens,
-                                int64_t dim, int64_t dim_out, int dtype, int trans_b) {
-  (void)trans_b;
-  Plan pl;
-  if (make_plan(batch_sizes, num_experts, num_tokens, dim, dim_out, dtype, pl) != GMM_OK) return 0;
-  return pl.split_bytes + pl.table_bytes;
-}
-
-int gmm_sm100_forward(const void* A, const void* B, const int64_t* batch_sizes, int64_t num_experts,
-                      int64_t num_tokens, int64_t dim, int64_t dim_out, int dtype, int trans_b,
-                      void* D, void* workspace, size_t workspace_bytes, void* stream_ptr) {
+int forward_impl(const void* A, const void* B, const int64_t* batch_sizes, int64_t num_experts,
+                 int64_t num_tokens, int64_t dim, int64_t dim_out, int dtype, int trans_b, void* D,
+                 void* workspace, size_t workspace_bytes, void* stream_ptr, const EpRoute* ep) {
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
   Plan pl;
   int rc = make_plan(batch_sizes, num_experts, num_tokens, dim, dim_out, dtype, pl);
@@ -685,9 +758,19 @@ int gmm_sm100_forward(const void* A, const void* B, const int64_t* batch_sizes, 
     return rc;
   const int64_t T = num_tokens, K = dim, N = dim_out, E = num_experts;
   if (T == 0 || N == 0) return GMM_OK;  // nothing to write
-  if (!D) return fail(GMM_ERR_INVALID_ARGUMENT, "D is null");
   const int es = elem_size(dtype);
-  if (!aligned16(D)) return fail(GMM_ERR_ALIGNMENT, "D must be 16-byte aligned");
+  if (ep) {
+    if (ep->world < 1 || ep->world > kMaxPeers || !ep->out_peers)
+      return fail(GMM_ERR_INVALID_ARGUMENT, "expert-parallel world must be 1.." + std::to_string(kMaxPeers));
+    for (int s = 0; s < ep->world; ++s)
+      if (!ep->out_peers[s] || !aligned16(ep->out_peers[s]))
+        return fail(GMM_ERR_ALIGNMENT, "every rank's output buffer must be non-null and 16-byte aligned");
+    if (K == 0) return fail(GMM_ERR_INVALID_ARGUMENT, "expert-parallel forward needs dim > 0");
+    if (!append_ep_table(pl, batch_sizes, E, *ep)) return fail(GMM_ERR_TOO_LARGE, "EP table too large");
+  } else {
+    if (!D) return fail(GMM_ERR_INVALID_ARGUMENT, "D is null");
+    if (!aligned16(D)) return fail(GMM_ERR_ALIGNMENT, "D must be 16-byte aligned");
+  }
   if ((N * es) % 16 != 0)
     return fail(GMM_ERR_ALIGNMENT, "dim_out * element size must be a multiple of 16 bytes, got dim_out=" +
                                        std::to_string(N));
@@ -720,6 +803,11 @@ int gmm_sm100_forward(const void* A, const void* B, const int64_t* batch_sizes, 
   prm.k_blocks = pl.k_blocks;
   prm.total_tiles = pl.total_tiles;
   prm.dim_out = static_cast<int>(N);
+  if (ep) {
+    prm.remote = 1;
+    prm.world = ep->world;
+    for (int s = 0; s < ep->world; ++s) prm.d_peer[s] = ep->out_peers[s];
+  }
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   if (pl.table_bytes == 0) {
     std::memcpy(prm.inline_table, pl.table.data(), pl.table.size() * sizeof(int32_t));
@@ -793,6 +881,129 @@ int gmm_sm100_forward(const void* A, const void* B, const int64_t* batch_sizes, 
                    : launch_variant<kKindBf16, true>(prm, grid, stream, di, 2);
   return trans_b ? launch_variant<kKindF16, false>(prm, grid, stream, di, 3)
                  : launch_variant<kKindF16, true>(prm, grid, stream, di, 4);
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* gmm_sm100_errstr(int status) {
+  switch (status) {
+    case GMM_OK: return "ok";
+    case GMM_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case GMM_ERR_BATCH_SUM: return "sum of batch_sizes does not match the number of rows";
+    case GMM_ERR_DTYPE: return "unsupported dtype";
+    case GMM_ERR_ALIGNMENT: return "misaligned pointer or row pitch";
+    case GMM_ERR_ARCH: return "unsupported GPU architecture (needs sm_100)";
+    case GMM_ERR_CUDA: return "CUDA error";
+    case GMM_ERR_WORKSPACE: return "workspace too small";
+    case GMM_ERR_TOO_LARGE: return "problem too large";
+    case GMM_ERR_DEVICE_TIMEOUT: return "device-side wait timed out";
+    default: return "unknown status";
+  }
+}
+
+const char* gmm_sm100_last_error(void) { return t_last_error.c_str(); }
+
+int gmm_sm100_check_device(int device) {
+  DeviceInfo* di = nullptr;
+  return device_info(device, &di);
+}
+
+size_t gmm_sm100_workspace_size(const int64_t* batch_sizes, int64_t num_experts, int64_t num_tokens,
+                                int64_t dim, int64_t dim_out, int dtype, int trans_b) {
+  (void)trans_b;
+  Plan pl;
+  if (make_plan(batch_sizes, num_experts, num_tokens, dim, dim_out, dtype, pl) != GMM_OK) return 0;
+  return pl.split_bytes + pl.table_bytes;
+}
+
+int gmm_sm100_forward(const void* A, const void* B, const int64_t* batch_sizes, int64_t num_experts,
+                      int64_t num_tokens, int64_t dim, int64_t dim_out, int dtype, int trans_b,
+                      void* D, void* workspace, size_t workspace_bytes, void* stream_ptr) {
+  return forward_impl(A, B, batch_sizes, num_experts, num_tokens, dim, dim_out, dtype, trans_b, D,
+                      workspace, workspace_bytes, stream_ptr, nullptr);
+}
+
+size_t gmm_sm100_ep_workspace_size(const int64_t* counts, int64_t num_local_experts, int world,
+                                   int64_t num_rows, int64_t dim, int64_t dim_out, int dtype) {
+  if (!counts || num_local_experts < 0 || world < 1 || world > kMaxPeers) return 0;
+  std::vector<int64_t> local_bs(static_cast<size_t>(num_local_experts), 0);
+  std::vector<int64_t> zeros(static_cast<size_t>(num_local_experts * world), 0);
+  for (int64_t e = 0; e < num_local_experts; ++e)
+    for (int s = 0; s < world; ++s) local_bs[e] += counts[e * world + s];
+  Plan pl;
+  if (make_plan(local_bs.data(), num_local_experts, num_rows, dim, dim_out, dtype, pl) != GMM_OK) return 0;
+  EpRoute route{world, nullptr, counts, zeros.data()};
+  if (!append_ep_table(pl, local_bs.data(), num_local_experts, route)) return 0;
+  return pl.split_bytes + pl.table_bytes;
+}
+
+int gmm_sm100_forward_ep(const void* X, const void* B, const int64_t* counts, const int64_t* dst_rows,
+                         int64_t num_local_experts, int world, void* const* out_peers,
+                         int64_t num_rows, int64_t dim, int64_t dim_out, int dtype, int trans_b,
+                         void* workspace, size_t workspace_bytes, void* stream) {
+  if (!counts || !dst_rows || num_local_experts < 0 || world < 1 || world > kMaxPeers)
+    return fail(GMM_ERR_INVALID_ARGUMENT, "bad expert-parallel routing arguments");
+  std::vector<int64_t> local_bs(static_cast<size_t>(num_local_experts), 0);
+  for (int64_t e = 0; e < num_local_experts; ++e)
+    for (int s = 0; s < world; ++s) {
+      if (counts[e * world + s] < 0) return fail(GMM_ERR_INVALID_ARGUMENT, "negative row count");
+      local_bs[e] += counts[e * world + s];
+    }
+  EpRoute route{world, out_peers, counts, dst_rows};
+  return forward_impl(X, B, local_bs.data(), num_local_experts, num_rows, dim, dim_out, dtype, trans_b,
+                      nullptr, workspace, workspace_bytes, stream, &route);
+}
+
+int gmm_sm100_ep_gather(void* X, const void* const* src_peers, const int64_t* counts,
+                        const int64_t* src_rows, int64_t num_local_experts, int world,
+                        int64_t row_bytes, void* stream_ptr) {
+  if (!counts || !src_rows || !src_peers || world < 1 || world > kMaxPeers || num_local_experts < 0)
+    return fail(GMM_ERR_INVALID_ARGUMENT, "bad gather arguments");
+  if (row_bytes <= 0 || row_bytes % 16 != 0)
+    return fail(GMM_ERR_ALIGNMENT, "row bytes must be a positive multiple of 16");
+  static_assert(sizeof(GatherParams) <= 32764, "kernel parameter limit");
+  GatherParams prm;
+  std::memset(&prm, 0, sizeof(prm));
+  int64_t rows = 0;
+  int n = 0;
+  for (int64_t e = 0; e < num_local_experts; ++e)
+    for (int s = 0; s < world; ++s) {
+      const int64_t m = counts[e * world + s];
+      if (m < 0 || src_rows[e * world + s] < 0) return fail(GMM_ERR_INVALID_ARGUMENT, "negative count or row");
+      if (m == 0) continue;
+      if (n >= kMaxGatherChunks) return fail(GMM_ERR_TOO_LARGE, "too many (expert, rank) chunks");
+      prm.chunk_dst[n] = static_cast<int>(rows);
+      prm.chunk_rank[n] = s;
+      prm.chunk_row[n] = static_cast<int>(src_rows[e * world + s]);
+      ++n;
+      rows += m;
+    }
+  if (rows == 0) return GMM_OK;
+  if (rows > INT32_MAX) return fail(GMM_ERR_TOO_LARGE, "too many rows");
+  if (!X || !aligned16(X)) return fail(GMM_ERR_ALIGNMENT, "X must be non-null and 16-byte aligned");
+  for (int s = 0; s < world; ++s) {
+    prm.src[s] = static_cast<const char*>(src_peers[s]);
+    if (prm.src[s] && !aligned16(prm.src[s])) return fail(GMM_ERR_ALIGNMENT, "source rows must be 16-byte aligned");
+  }
+  for (int c = 0; c < n; ++c)
+    if (!prm.src[prm.chunk_rank[c]]) return fail(GMM_ERR_INVALID_ARGUMENT, "null source pointer");
+  prm.chunk_dst[n] = static_cast<int>(rows);
+  prm.x = static_cast<char*>(X);
+  prm.row_bytes = row_bytes;
+  prm.n_chunks = n;
+  prm.total_rows = static_cast<int>(rows);
+  int dev = 0;
+  cudaError_t ce = cudaGetDevice(&dev);
+  if (ce != cudaSuccess) return cuda_fail(ce, "cudaGetDevice");
+  DeviceInfo* di = nullptr;
+  int rc = device_info(dev, &di);
+  if (rc != GMM_OK) return rc;
+  const int blocks = static_cast<int>(std::min<int64_t>((rows + 7) / 8, 4LL * di->sm_count));
+  ep_gather_kernel<<<std::max(blocks, 1), 256, 0, static_cast<cudaStream_t>(stream_ptr)>>>(prm);
+  ce = cudaGetLastError();
+  return ce == cudaSuccess ? GMM_OK : cuda_fail(ce, "ep gather launch");
 }
 
 int gmm_sm100_device_error(int* status_out, int clear) {

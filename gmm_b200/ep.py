@@ -23,6 +23,22 @@ c+1's GEMM runs on the compute stream.  Every rank derives every owner's
 chunking from the gathered counts, so both ends of each message agree on
 which batch carries it.
 
+Two transports carry steps 2 and 4:
+
+* ``"direct"`` (default on GPUs, up to 8 ranks): every rank's token rows and
+  output rows live in symmetric memory (``torch.distributed._symmetric_memory``),
+  so each rank can address its peers' buffers over NVLink.  Dispatch is one
+  gather kernel pulling each (expert, source) chunk into the expert-major
+  receive buffer with peer loads; the combine is fused into the grouped-GEMM
+  epilogue, which stores each result row straight into the output buffer of
+  the rank it came from, tile by tile, while the next tiles are computed.
+  Two 1-element NCCL all-reduces on the compute stream order the step: inputs
+  written everywhere before the gather, all peer stores landed before the
+  output is read.  The returned tensor is a view of this rank's symmetric
+  output buffer, valid until the next call.
+* ``"nccl"``: NCCL point-to-point messages (below); also what the CPU tests
+  run on gloo ranks.
+
 Rank r owns experts ``[r*E/W, (r+1)*E/W)``.  Output rows are bit-identical
 to the single-GPU operator on the same rows.  There is no CPU fallback: the
 local GEMM is the CUDA kernel (through the C ABI, writing in place into a
@@ -84,12 +100,19 @@ class ExpertParallelGmm:
             from the world if not given.
         local_gemm: ``f(a, b_local, batch_sizes, trans_b) -> d`` replacing the CUDA
             kernel (tests only: checks the exchange logic on CPU ranks).
-        chunks: pipeline depth (GEMM / combine overlap); default 1 (measured fastest
-            with NCCL point-to-point on 2 B200s).
+        chunks: pipeline depth of the ``"nccl"`` transport (GEMM / combine overlap);
+            default 1 (measured fastest with NCCL point-to-point on 2 B200s).
+        transport: ``"direct"``, ``"nccl"`` or ``"auto"`` (direct for CUDA tensors on
+            up to 8 ranks without a substituted ``local_gemm``).
     """
 
     def __init__(self, num_experts: int, group=None, count_group=None,
-                 local_gemm: Optional[Callable] = None, chunks: int = 1):
+                 local_gemm: Optional[Callable] = None, chunks: int = 1, transport: str = "auto"):
+        if transport not in ("auto", "direct", "nccl"):
+            raise ValueError(f"unknown transport {transport!r}")
+        self.transport = transport
+        self._sym = None  # (capacity rows, dim, dim_out, dtype, device, a_sym, out_sym, a_ptrs, out_ptrs)
+        self._flag = None
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -138,6 +161,79 @@ class ExpertParallelGmm:
         from gmm_b200 import capi
         capi.forward(x, b, bs_list, y, trans_b=trans_b)
 
+    # ------------------------------------------------------- direct transport
+    def _use_direct(self, a: torch.Tensor) -> bool:
+        if self.transport == "nccl" or self.local_gemm is not None:
+            return False
+        ok = a.is_cuda and self.world <= 8
+        if self.transport == "direct" and not ok:
+            raise ValueError("the direct transport needs CUDA tensors and at most 8 ranks")
+        return ok
+
+    def _barrier(self, device):
+        if self._flag is None or self._flag.device != device:
+            self._flag = torch.zeros(1, dtype=torch.float32, device=device)
+        dist.all_reduce(self._flag, group=self.group)
+
+    def _symmetric(self, rows: int, dim: int, dim_out: int, dtype, device):
+        """(Re)allocate the symmetric token / output buffers; collective when it allocates.
+
+        Every rank derives ``rows`` from the same gathered counts, so all ranks
+        (re)allocate together."""
+        import torch.distributed._symmetric_memory as symm_mem
+        cur = self._sym
+        if cur is not None and cur[0] >= rows and cur[1:5] == (dim, dim_out, dtype, device):
+            return cur
+        cap = max(rows, 1)
+        cap = (cap + 1023) // 1024 * 1024
+        group = self.group if self.group is not None else dist.group.WORLD
+        a_sym = symm_mem.empty(cap * dim, dtype=dtype, device=device)
+        h_a = symm_mem.rendezvous(a_sym, group)
+        o_sym = symm_mem.empty(cap * dim_out, dtype=dtype, device=device)
+        h_o = symm_mem.rendezvous(o_sym, group)
+        self._sym = (cap, dim, dim_out, dtype, device, a_sym, o_sym,
+                     list(h_a.buffer_ptrs), list(h_o.buffer_ptrs), h_a, h_o)
+        return self._sym
+
+    def input_buffer(self, rows: int, dim: int, dim_out: int, dtype, device) -> torch.Tensor:
+        """A ``[rows, dim]`` view of this rank's symmetric token buffer.
+
+        Writing the layer's input rows here (instead of passing any tensor)
+        saves the copy into symmetric memory in ``forward``.  Collective: every
+        rank must call it with the same capacity."""
+        sym = self._symmetric(rows, dim, dim_out, dtype, device)
+        return sym[5][:rows * dim].view(rows, dim)
+
+    def _forward_direct(self, a, b_local, bs, trans_b):
+        from gmm_b200 import capi
+        W, El, r = self.world, self.e_local, self.rank
+        dim = a.shape[1]
+        dim_out = b_local.shape[1] if trans_b else b_local.shape[2]
+        rows_max = max(sum(row) for row in bs)
+        sym = self._symmetric(rows_max, dim, dim_out, a.dtype, a.device)
+        a_sym = sym[5][:a.shape[0] * dim].view(a.shape[0], dim)
+        out = sym[6][:a.shape[0] * dim_out].view(a.shape[0], dim_out)
+        if a.data_ptr() != a_sym.data_ptr():
+            a_sym.copy_(a)
+        # offsets of every global expert's rows in every rank's layout
+        offs = []
+        for s in range(W):
+            o, row = 0, []
+            for g in range(self.num_experts):
+                row.append(o)
+                o += bs[s][g]
+            offs.append(row)
+        counts = [bs[s][r * El + e] for e in range(El) for s in range(W)]
+        rows_at = [offs[s][r * El + e] for e in range(El) for s in range(W)]
+        n_recv = sum(counts)
+        x = self._buffer("_x", n_recv, dim, a)
+        self._barrier(a.device)  # every rank's token rows are in place
+        if n_recv:
+            capi.ep_gather(x, sym[7], counts, rows_at, El, dim * a.element_size())
+            capi.forward_ep(x, b_local, counts, rows_at, El, sym[8], trans_b=trans_b)
+        self._barrier(a.device)  # every peer's result rows have landed here
+        return out
+
     # --------------------------------------------------------------- forward
     def forward(self, a: torch.Tensor, b_local: torch.Tensor, batch_sizes: torch.Tensor,
                 trans_b: bool = False, all_bs: Optional[torch.Tensor] = None) -> torch.Tensor:
@@ -160,6 +256,8 @@ class ExpertParallelGmm:
         if all_bs is None:
             all_bs = self.exchange_counts(batch_sizes)
         bs = all_bs.tolist()
+        if self._use_direct(a):
+            return self._forward_direct(a, b_local, bs, trans_b)
         ch = _Chunking(bs, W, El, self.chunks)
         C = ch.chunks
         dim = a.shape[1]

@@ -76,10 +76,17 @@ def run(args, metric, load_peaks, clock_sampler):
         El = E // world
         bs, tokens_r, tokens_total, weak = _routing(cfg, world, rank)
         rows_r = int(bs.sum())
-        g = torch.Generator(device=dev).manual_seed(cfg.seed * 7919 + rank)
-        a = torch.randn(rows_r, cfg.dim, generator=g, device=dev).to(cfg.dtype)
         b_local = _local_weights(cfg, list(range(rank * El, (rank + 1) * El)), dev)
-        ep = ExpertParallelGmm(E, count_group=count_group)
+        ep = ExpertParallelGmm(E, count_group=count_group,
+                               transport=os.environ.get("GMM_EP_TRANSPORT", "auto"))
+        all_bs = ep.exchange_counts(bs)
+        g = torch.Generator(device=dev).manual_seed(cfg.seed * 7919 + rank)
+        if ep._use_direct(b_local):
+            # the layer's input rows live in this rank's symmetric token buffer
+            a = ep.input_buffer(int(all_bs.sum(1).max()), cfg.dim, cfg.dim_out, cfg.dtype, dev)[:rows_r]
+            a.copy_(torch.randn(rows_r, cfg.dim, generator=g, device=dev))
+        else:
+            a = torch.randn(rows_r, cfg.dim, generator=g, device=dev).to(cfg.dtype)
 
         rows_all = torch.tensor([rows_r], dtype=torch.float64, device=dev)
         dist.all_reduce(rows_all)
@@ -109,7 +116,7 @@ def run(args, metric, load_peaks, clock_sampler):
         # e2e: A_r and this rank's expert weights from pinned host memory, out back to host
         a_h = a.cpu().pin_memory()
         b_h = b_local.cpu().pin_memory()
-        a_d, b_d = torch.empty_like(a), torch.empty_like(b_local)
+        a_d, b_d = a, torch.empty_like(b_local)  # inputs land where the layer reads them
         out_h = torch.empty(rows_r, cfg.dim_out, dtype=cfg.dtype).pin_memory()
 
         def e2e_step():
@@ -156,7 +163,10 @@ def run(args, metric, load_peaks, clock_sampler):
                            "rows": int(rows_all.item()), "trans_b": cfg.trans_b,
                            "parallelism": f"ep{world}",
                            "l2": "inputs larger than L2 (126 MB)",
-                           "exchange": "gloo count all-gather + NCCL P2P dispatch/combine"},
+                           "exchange": ("gloo count all-gather; NVLink peer-load gather + combine "
+                                        "fused into the GEMM epilogue (symmetric memory)")
+                           if ep._use_direct(b_local) else
+                           "gloo count all-gather + NCCL P2P dispatch/combine"},
                 "e2e": {"value": round(flops / (ems.item() * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
                         "ms_per_step": round(ems.item(), 3),
                         "h2d_bytes_per_step": int(h2d.item()), "d2h_bytes_per_step": int(d2h.item()),

@@ -88,6 +88,35 @@ int gmm_sm100_forward(const void* A, const void* B, const int64_t* batch_sizes,
  * reference kernel has no device-side error path). */
 int gmm_sm100_device_error(int* status_out, int clear);
 
+/* ---------------------------------------------------------------- expert parallelism
+ * No reference counterpart (the reference runs on one GPU).  A rank owning
+ * num_local_experts experts receives, for local expert e, counts[e*world + s]
+ * rows from each source rank s, stored expert-major in X (all sources of
+ * expert 0, then of expert 1, ...).  The pointers in out_peers / src_peers are
+ * device addresses valid on the calling device (peer memory of the other
+ * ranks, e.g. symmetric-memory buffers); world <= 8. */
+
+/* Dispatch: copy every (expert, source) chunk of rows into X, reading
+ * src_peers[s] + src_rows[e*world + s] * row_bytes over NVLink. */
+int gmm_sm100_ep_gather(void* X, const void* const* src_peers, const int64_t* counts,
+                        const int64_t* src_rows, int64_t num_local_experts, int world,
+                        int64_t row_bytes, void* stream);
+
+/* Local grouped GEMM with the combine fused into its epilogue: the result of
+ * each row of X goes straight to row dst_rows[e*world + s] + i of
+ * out_peers[s] (the rank the row came from).  B holds the local experts'
+ * weights ([E_local, dim, dim_out], or [E_local, dim_out, dim] if trans_b).
+ * The caller orders the peers' reads/writes with a cross-rank barrier
+ * before and after. */
+int gmm_sm100_forward_ep(const void* X, const void* B, const int64_t* counts, const int64_t* dst_rows,
+                         int64_t num_local_experts, int world, void* const* out_peers,
+                         int64_t num_rows, int64_t dim, int64_t dim_out, int dtype, int trans_b,
+                         void* workspace, size_t workspace_bytes, void* stream);
+
+/* Workspace bytes gmm_sm100_forward_ep needs (fp32 splits, large tables). */
+size_t gmm_sm100_ep_workspace_size(const int64_t* counts, int64_t num_local_experts, int world,
+                                   int64_t num_rows, int64_t dim, int64_t dim_out, int dtype);
+
 /* Size of the fixed scratch area used by gmm_sm100_forward_f32_noalloc. */
 #define GMM_SM100_NOALLOC_SCRATCH_BYTES (8u << 20) /* 8 MiB */
 

@@ -22,7 +22,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, E, dtype, trans_b):
+def _worker(rank, world, port, E, dtype, trans_b, transport):
     import sys
     sys.path.insert(0, ROOT)
     torch.cuda.set_device(rank)
@@ -43,21 +43,26 @@ def _worker(rank, world, port, E, dtype, trans_b):
         shape = (E, dim_out, dim) if trans_b else (E, dim, dim_out)
         b_full = (torch.randn(*shape, generator=gb) / dim ** 0.5).to(dtype).to(dev)
         El = E // world
-        ep = ExpertParallelGmm(E)
-        out = ep(a, b_full[rank * El:(rank + 1) * El].contiguous(), bs, trans_b)
+        ep = ExpertParallelGmm(E, transport=transport)
+        b_local = b_full[rank * El:(rank + 1) * El].contiguous()
         want = hopper_gmm_fwd(a, b_full, bs, trans_b=trans_b)
-        torch.cuda.synchronize()
-        assert torch.equal(out, want), f"rank {rank}: EP differs from the single-GPU op"
+        for step in range(2):  # a second step reuses every buffer
+            out = ep(a, b_local, bs, trans_b)
+            torch.cuda.synchronize()
+            assert torch.equal(out, want), f"rank {rank} step {step}: EP differs from the single-GPU op"
         dist.barrier()
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("E,dtype,trans_b", [(8, torch.bfloat16, False), (16, torch.float16, True)])
-def test_ep_nccl_matches_single_gpu(E, dtype, trans_b):
+@pytest.mark.parametrize("transport", ["direct", "nccl"])
+@pytest.mark.parametrize("E,dtype,trans_b", [(8, torch.bfloat16, False), (16, torch.float16, True),
+                                             (8, torch.float32, False)])
+def test_ep_matches_single_gpu(E, dtype, trans_b, transport):
     n = torch.cuda.device_count() if torch.cuda.is_available() else 0
     if n < 2:
         pytest.skip("needs 2 GPUs")
     world = 2 if n < 4 else 4
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
-    mp.spawn(_worker, args=(world, _free_port(), E, dtype, trans_b), nprocs=world, join=True)
+    mp.spawn(_worker, args=(world, _free_port(), E, dtype, trans_b, transport), nprocs=world,
+             join=True)
