@@ -78,4 +78,13 @@ if _HAS_C:
         return torch.empty(num_tokens, n, dtype=a.dtype, device=a.device)
 
 
+def hopper_gmm_fwd_host(a, b, batch_sizes, trans_b=False, out=None, device=None):
+    """``hopper_gmm_fwd`` on host-resident (pinned) operands, with the transfers pipelined
+    against the GEMM; see :mod:`gmm_b200.streaming`."""
+    if not _HAS_C:
+        raise RuntimeError("gmm_b200._C is not available. Build with `python -m gmm_b200.build`.")
+    from gmm_b200.streaming import hopper_gmm_fwd_host as _f
+    return _f(a, b, batch_sizes, trans_b=trans_b, out=out, device=device)
+
+
 __all__ = ["hopper_gmm_fwd"]

@@ -212,3 +212,21 @@ def test_config2_checksum_of_checksums():
     # bf16 rounding of 14336 outputs per row: error ~ sqrt(N) * ulp/2 * |d|
     tol = 4.0 * math.sqrt(cfg.dim_out) * 2 ** -8 * out.float().abs().mean().item() + 1e-2
     assert (got - want).abs().max().item() < tol
+
+
+@pytest.mark.parametrize("dtype,trans_b", [(torch.bfloat16, False), (torch.float16, True),
+                                           (torch.float32, False)])
+def test_host_streamed_matches_device_op(dtype, trans_b):
+    """hopper_gmm_fwd_host (pipelined PCIe transfers) gives the device op's bytes."""
+    from gmm_b200 import hopper_gmm_fwd, hopper_gmm_fwd_host
+    g = torch.Generator().manual_seed(9)
+    bs = torch.tensor([300, 0, 17, 512, 1, 0, 260, 99, 4])
+    T, dim, dim_out = int(bs.sum()), 256, 384
+    a = torch.randn(T, dim, generator=g).to(dtype).pin_memory()
+    shape = (len(bs), dim_out, dim) if trans_b else (len(bs), dim, dim_out)
+    b = (torch.randn(*shape, generator=g) / 16).to(dtype).pin_memory()
+    want = hopper_gmm_fwd(a.cuda(), b.cuda(), bs, trans_b=trans_b).cpu()
+    for _ in range(2):  # the second call reuses the pipeline's buffers
+        got = hopper_gmm_fwd_host(a, b, bs, trans_b=trans_b)
+        torch.cuda.synchronize()
+        assert torch.equal(got, want)
