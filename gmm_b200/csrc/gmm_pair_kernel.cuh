@@ -35,7 +35,8 @@ struct PairCfg {
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = 2 * BN;
   static constexpr uint32_t kIdesc = make_idesc(kKind == kKindBf16 ? 1u : 0u, kBMnMajor, BM, BN);
-  static constexpr int kSmemBytes = kStages * kStageBytes + 256 + 1024;
+  static constexpr int kBarBytes = 256;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kBarBytes + kEpiStageBytes + 1024;
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
 
@@ -65,6 +66,7 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_pair_kernel(const __grid_cons
   uint64_t* drain_bar = bars + 2 * C::kStages + 4;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * C::kStages + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint8_t* epi_stage = smem + C::kStages * C::kStageBytes + C::kBarBytes;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
@@ -185,7 +187,7 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_pair_kernel(const __grid_cons
     // ------------------------------------------------------------ epilogue (both CTAs)
     using OutT = typename std::conditional<kKind == kKindBf16, __nv_bfloat16, __half>::type;
     const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;
+    const uint32_t stage = smem_u32(epi_stage) + quarter * (32 * 128);
     const uint32_t tempty_leader0 = map_shared_to_rank(smem_u32(tempty_bar), 0);
     int g = 0;
     int local = 0;
@@ -199,29 +201,8 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_pair_kernel(const __grid_cons
       const int row0 = t.row0 + C::BM_CTA * static_cast<int>(cta);
       if (quarter * 32 < rows_cta) {  // warp-uniform
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * C::BN;
-        const bool row_live = r < rows_cta;
-        OutT* drow = row_live ? out_row<OutT>(p, tv, g, row0 + r) : nullptr;
-#pragma unroll 1
-        for (int c = 0; c < C::BN / 32; ++c) {
-          const int col = t.n0 + c * 32;
-          if (col >= p.dim_out) break;  // warp-uniform
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(taddr + c * 32, v);
-          tmem_wait_ld();
-          if (!row_live) continue;
-          OutT* out = drow + col;
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            if (col + q * 8 < p.dim_out) {
-              uint4 pk;
-              pk.x = pack2<OutT>(__uint_as_float(v[8 * q + 0]), __uint_as_float(v[8 * q + 1]));
-              pk.y = pack2<OutT>(__uint_as_float(v[8 * q + 2]), __uint_as_float(v[8 * q + 3]));
-              pk.z = pack2<OutT>(__uint_as_float(v[8 * q + 4]), __uint_as_float(v[8 * q + 5]));
-              pk.w = pack2<OutT>(__uint_as_float(v[8 * q + 6]), __uint_as_float(v[8 * q + 7]));
-              *reinterpret_cast<uint4*>(out + q * 8) = pk;
-            }
-          }
-        }
+        drain_slab<OutT, C::BN>(p, tv, g, row0 + quarter * 32, min(32, rows_cta - quarter * 32), t.n0,
+                                taddr, stage, lane);
       }
       tc_fence_before();
       __syncwarp();

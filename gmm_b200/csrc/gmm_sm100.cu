@@ -47,6 +47,7 @@ constexpr int kInlineTableInts = 3 * kInlineGroups + 2;
 constexpr int kMaxPeers = 8;         // expert-parallel ranks a kernel can address
 constexpr int kMBlock = 16;          // m-tiles per raster block (L2 reuse of B columns)
 constexpr int kThreads = 256;        // 8 warps: TMA, MMA, TMEM alloc, idle, 4x epilogue
+constexpr int kEpiStageBytes = 4 * 32 * 128;  // epilogue staging: 4 warps x 32 rows x 128 B
 
 struct __align__(64) GmmParams {
   CUtensorMap tmap_a;   // A, or A_hi for fp32
@@ -95,7 +96,7 @@ struct Cfg {
   static constexpr uint32_t kIdesc =
       make_idesc(kTf32 ? 2u : (kKind == kKindBf16 ? 1u : 0u), kBMnMajor, BM, BN);
   static constexpr int kBarBytes = 256;
-  static constexpr int kSmemBytes = kStages * kStageBytes + kBarBytes + 1024;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kBarBytes + kEpiStageBytes + 1024;
   static_assert(!(kTf32 && kBMnMajor), "fp32 B is staged K-major by the split pre-pass");
   static_assert(kABytes % 1024 == 0 && kBBytes % 1024 == 0, "swizzle atoms need 1 KB alignment");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
@@ -185,6 +186,64 @@ __device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// Drains one 32-row slab of an accumulator -- TMEM lanes [32q, 32q + 32) of
+// columns [taddr, taddr + BN) -- into its output rows.  Each thread converts its
+// own row; the rows then pass through `stage` (32 rows x 128 B, 16-byte chunks
+// XOR-swizzled by row, conflict-free both ways) so that every store
+// instruction writes four whole 128-byte row segments (8 lanes per row): full
+// L2 lines locally, and large NVLink writes when the row lives on a peer.
+template <typename OutT, int BN>
+__device__ __forceinline__ void drain_slab(const GmmParams& p, const TableView& tv, int g,
+                                           int slab_row0, int slab_rows, int n0, uint32_t taddr,
+                                           uint32_t stage, int lane) {
+  constexpr int kColsPerSeg = 128 / static_cast<int>(sizeof(OutT));  // 64 (16-bit) or 32 (fp32)
+  constexpr int kElemsPer16 = 16 / static_cast<int>(sizeof(OutT));
+  OutT* rp[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int rr = i * 4 + (lane >> 3);
+    rp[i] = rr < slab_rows ? out_row<OutT>(p, tv, g, slab_row0 + rr) : nullptr;
+  }
+  const int ch = lane & 7;
+  const uint32_t my_row = stage + lane * 128;
+#pragma unroll 1
+  for (int c0 = 0; c0 < BN; c0 += kColsPerSeg) {
+    const int col = n0 + c0;
+    if (col >= p.dim_out) break;  // warp-uniform
+#pragma unroll
+    for (int h = 0; h < kColsPerSeg / 32; ++h) {
+      uint32_t v[32];
+      tmem_ld_32x32b_x32(taddr + c0 + h * 32, v);
+      tmem_wait_ld();
+      if constexpr (sizeof(OutT) == 2) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint4 pk;
+          pk.x = pack2<OutT>(__uint_as_float(v[8 * q + 0]), __uint_as_float(v[8 * q + 1]));
+          pk.y = pack2<OutT>(__uint_as_float(v[8 * q + 2]), __uint_as_float(v[8 * q + 3]));
+          pk.z = pack2<OutT>(__uint_as_float(v[8 * q + 4]), __uint_as_float(v[8 * q + 5]));
+          pk.w = pack2<OutT>(__uint_as_float(v[8 * q + 6]), __uint_as_float(v[8 * q + 7]));
+          st_shared_v4(my_row + (((h * 4 + q) ^ (lane & 7)) << 4), pk);
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          st_shared_v4(my_row + ((q ^ (lane & 7)) << 4),
+                       make_uint4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
+      }
+    }
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int rr = i * 4 + (lane >> 3);
+      const uint4 val = ld_shared_v4(stage + rr * 128 + ((ch ^ (rr & 7)) << 4));
+      if (rp[i] && col + ch * kElemsPer16 < p.dim_out)
+        *reinterpret_cast<uint4*>(rp[i] + col + ch * kElemsPer16) = val;
+    }
+    __syncwarp();
+  }
+}
+
 template <int kKind, bool kBMnMajor>
 __global__ void __launch_bounds__(kThreads, 1) gmm_persistent_kernel(const __grid_constant__ GmmParams p) {
   using C = Cfg<kKind, kBMnMajor>;
@@ -202,6 +261,7 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_persistent_kernel(const __gri
   uint64_t* drain_bar = bars + 2 * C::kStages + 4;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * C::kStages + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint8_t* epi_stage = smem + C::kStages * C::kStageBytes + C::kBarBytes;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
@@ -340,8 +400,10 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_persistent_kernel(const __gri
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ epilogue
+    using OutT = typename std::conditional<C::kTf32, float,
+        typename std::conditional<kKind == kKindBf16, __nv_bfloat16, __half>::type>::type;
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
-    const int r = quarter * 32 + lane;
+    const uint32_t stage = smem_u32(epi_stage) + quarter * (32 * 128);
     int g = 0;
     int local = 0;
     for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, ++local) {
@@ -352,43 +414,8 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_persistent_kernel(const __gri
       const Tile t = decode_tile<C::BM, C::BN>(tv, n_tiles, tile, g);
       if (quarter * 32 < t.rows) {  // warp-uniform: some row of this quarter is live
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * C::BN;
-        const bool row_live = r < t.rows;
-        using RowT = typename std::conditional<C::kTf32, float,
-            typename std::conditional<kKind == kKindBf16, __nv_bfloat16, __half>::type>::type;
-        RowT* drow = row_live ? out_row<RowT>(p, tv, g, t.row0 + r) : nullptr;
-#pragma unroll 1
-        for (int c = 0; c < C::BN / 32; ++c) {
-          const int col = t.n0 + c * 32;
-          if (col >= p.dim_out) break;  // warp-uniform
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(taddr + c * 32, v);
-          tmem_wait_ld();
-          if (!row_live) continue;
-          if (C::kTf32) {
-            float* out = reinterpret_cast<float*>(drow) + col;
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              if (col + q * 4 < p.dim_out) {
-                uint4 pk = make_uint4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-                *reinterpret_cast<uint4*>(out + q * 4) = pk;
-              }
-            }
-          } else {
-            using OutT = typename std::conditional<kKind == kKindBf16, __nv_bfloat16, __half>::type;
-            OutT* out = reinterpret_cast<OutT*>(drow) + col;
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              if (col + q * 8 < p.dim_out) {
-                uint4 pk;
-                pk.x = pack2<OutT>(__uint_as_float(v[8 * q + 0]), __uint_as_float(v[8 * q + 1]));
-                pk.y = pack2<OutT>(__uint_as_float(v[8 * q + 2]), __uint_as_float(v[8 * q + 3]));
-                pk.z = pack2<OutT>(__uint_as_float(v[8 * q + 4]), __uint_as_float(v[8 * q + 5]));
-                pk.w = pack2<OutT>(__uint_as_float(v[8 * q + 6]), __uint_as_float(v[8 * q + 7]));
-                *reinterpret_cast<uint4*>(out + q * 8) = pk;
-              }
-            }
-          }
-        }
+        drain_slab<OutT, C::BN>(p, tv, g, t.row0 + quarter * 32, min(32, t.rows - quarter * 32), t.n0,
+                                taddr, stage, lane);
       }
       tc_fence_before();
       __syncwarp();
