@@ -62,7 +62,7 @@ def test_ep_matches_single_gpu(E, dtype, trans_b, transport):
     n = torch.cuda.device_count() if torch.cuda.is_available() else 0
     if n < 2:
         pytest.skip("needs 2 GPUs")
-    world = 2 if n < 4 else 4
+    world = min(n, 8)
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     mp.spawn(_worker, args=(world, _free_port(), E, dtype, trans_b, transport), nprocs=world,
              join=True)
