@@ -20,9 +20,11 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
 def _free_port():
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
+    """A fresh rendezvous file (no TCP port, so no port races between tests)."""
+    fd, path = tempfile.mkstemp(prefix="gmm_rdzv_")
+    os.close(fd)
+    os.unlink(path)
+    return path
 
 
 def _oracle_local_gemm(a, b, bs, trans_b):
@@ -51,7 +53,7 @@ def _rank_inputs(rank, E, dim, dim_out, trans_b, skew):
 def _ep_worker(rank, world, port, E, trans_b, skew, chunks):
     import sys
     sys.path.insert(0, ROOT)
-    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+    dist.init_process_group("gloo", init_method=f"file://{port}", rank=rank,
                             world_size=world, timeout=datetime.timedelta(seconds=60))
     try:
         import oracle
@@ -89,7 +91,7 @@ def _dropout_worker(rank, world, port, outdir):
     import sys
     import time
     sys.path.insert(0, ROOT)
-    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+    dist.init_process_group("gloo", init_method=f"file://{port}", rank=rank,
                             world_size=world, timeout=datetime.timedelta(seconds=3))
     if rank == 1:
         # this rank leaves between steps: it never joins the exchange
@@ -125,7 +127,7 @@ def test_dropped_rank_is_detected_not_hung():
 def test_ep_rejects_bad_inputs():
     from gmm_b200.ep import ExpertParallelGmm
     port = _free_port()
-    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1)
+    dist.init_process_group("gloo", init_method=f"file://{port}", rank=0, world_size=1)
     try:
         ep = ExpertParallelGmm(4, local_gemm=_oracle_local_gemm)
         with pytest.raises(ValueError, match="Sum of batch_sizes"):

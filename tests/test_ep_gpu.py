@@ -6,6 +6,7 @@ from the same operands, only its neighbours in the tile differ."""
 import datetime
 import os
 import socket
+import tempfile
 
 import pytest
 import torch
@@ -17,9 +18,11 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
 def _free_port():
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
+    """A fresh rendezvous file (no TCP port, so no port races between tests)."""
+    fd, path = tempfile.mkstemp(prefix="gmm_rdzv_")
+    os.close(fd)
+    os.unlink(path)
+    return path
 
 
 def _worker(rank, world, port, E, dtype, trans_b, transport):
@@ -27,7 +30,7 @@ def _worker(rank, world, port, E, dtype, trans_b, transport):
     sys.path.insert(0, ROOT)
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
-    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+    dist.init_process_group("nccl", init_method=f"file://{port}", rank=rank,
                             world_size=world, timeout=datetime.timedelta(seconds=60), device_id=dev)
     try:
         from gmm_b200 import hopper_gmm_fwd
