@@ -204,28 +204,23 @@ class ExpertParallelGmm:
         sym = self._symmetric(rows, dim, dim_out, dtype, device)
         return sym[5][:rows * dim].view(rows, dim)
 
-    def _forward_direct(self, a, b_local, bs, trans_b):
+    def _forward_direct(self, a, b_local, all_bs, trans_b):
         from gmm_b200 import capi
         W, El, r = self.world, self.e_local, self.rank
         dim = a.shape[1]
         dim_out = b_local.shape[1] if trans_b else b_local.shape[2]
-        rows_max = max(sum(row) for row in bs)
+        rows_max = int(all_bs.sum(1).max())
         sym = self._symmetric(rows_max, dim, dim_out, a.dtype, a.device)
         a_sym = sym[5][:a.shape[0] * dim].view(a.shape[0], dim)
         out = sym[6][:a.shape[0] * dim_out].view(a.shape[0], dim_out)
         if a.data_ptr() != a_sym.data_ptr():
             a_sym.copy_(a)
-        # offsets of every global expert's rows in every rank's layout
-        offs = []
-        for s in range(W):
-            o, row = 0, []
-            for g in range(self.num_experts):
-                row.append(o)
-                o += bs[s][g]
-            offs.append(row)
-        counts = [bs[s][r * El + e] for e in range(El) for s in range(W)]
-        rows_at = [offs[s][r * El + e] for e in range(El) for s in range(W)]
-        n_recv = sum(counts)
+        # offsets of every global expert's rows in every rank's layout: [W, E]
+        offs = torch.cumsum(all_bs, dim=1) - all_bs
+        mine = slice(r * El, (r + 1) * El)
+        counts = all_bs[:, mine].t().contiguous().numpy()   # [El, W]: rows of local e from s
+        rows_at = offs[:, mine].t().contiguous().numpy()    # where they sit on s
+        n_recv = int(counts.sum())
         x = self._buffer("_x", n_recv, dim, a)
         self._barrier(a.device)  # every rank's token rows are in place
         if n_recv:
@@ -255,9 +250,9 @@ class ExpertParallelGmm:
                              f"A.size(0) ({a.shape[0]})")
         if all_bs is None:
             all_bs = self.exchange_counts(batch_sizes)
-        bs = all_bs.tolist()
         if self._use_direct(a):
-            return self._forward_direct(a, b_local, bs, trans_b)
+            return self._forward_direct(a, b_local, all_bs, trans_b)
+        bs = all_bs.tolist()
         ch = _Chunking(bs, W, El, self.chunks)
         C = ch.chunks
         dim = a.shape[1]
