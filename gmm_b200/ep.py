@@ -104,10 +104,14 @@ class ExpertParallelGmm:
             default 1 (measured fastest with NCCL point-to-point on 2 B200s).
         transport: ``"direct"``, ``"nccl"`` or ``"auto"`` (direct for CUDA tensors on
             up to 8 ranks without a substituted ``local_gemm``).
+        count_exchange: ``"shm"`` (shared memory, ranks on one host), ``"gloo"``, or
+            ``"auto"`` (shm when every rank is on this host).  Construction is
+            collective over the count group.
     """
 
     def __init__(self, num_experts: int, group=None, count_group=None,
-                 local_gemm: Optional[Callable] = None, chunks: int = 1, transport: str = "auto"):
+                 local_gemm: Optional[Callable] = None, chunks: int = 1, transport: str = "auto",
+                 count_exchange: str = "auto"):
         if transport not in ("auto", "direct", "nccl"):
             raise ValueError(f"unknown transport {transport!r}")
         self.transport = transport
@@ -130,6 +134,13 @@ class ExpertParallelGmm:
                       for i in range(self.world)]
         self._x = None
         self._y = None
+        self._shm_counts = None
+        if count_exchange not in ("auto", "shm", "gloo"):
+            raise ValueError(f"unknown count_exchange {count_exchange!r}")
+        if count_exchange != "gloo" and self.world > 1:
+            from gmm_b200.host_exchange import ShmCountExchange, same_host
+            if count_exchange == "shm" or same_host(self.count_group):
+                self._shm_counts = ShmCountExchange(num_experts, self.count_group)
 
     # ------------------------------------------------------------------ plan
     def exchange_counts(self, batch_sizes: torch.Tensor) -> torch.Tensor:
@@ -139,6 +150,8 @@ class ExpertParallelGmm:
             raise ValueError("batch_sizes must be a 1D CPU int64 tensor with num_experts entries")
         if (batch_sizes < 0).any():
             raise ValueError("batch_sizes must be non-negative")
+        if self._shm_counts is not None:
+            return self._shm_counts(batch_sizes.contiguous())
         out = [torch.empty_like(batch_sizes) for _ in range(self.world)]
         dist.all_gather(out, batch_sizes.contiguous(), group=self.count_group)
         return torch.stack(out)

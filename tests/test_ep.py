@@ -140,3 +140,39 @@ def test_ep_rejects_bad_inputs():
         assert torch.equal(out, torch.full((3, 2), 8.0))
     finally:
         dist.destroy_process_group()
+
+
+def _shm_worker(rank, world, path, outdir):
+    import sys
+    import time
+    sys.path.insert(0, ROOT)
+    dist.init_process_group("gloo", init_method=f"file://{path}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=30))
+    from gmm_b200.host_exchange import ShmCountExchange
+    ex = ShmCountExchange(5, timeout_s=2.0)
+    for step in range(3):  # a few steps through both slots
+        got = ex(torch.arange(5, dtype=torch.int64) * (rank + 1) + step)
+        want = torch.stack([torch.arange(5) * (r + 1) + step for r in range(world)])
+        assert torch.equal(got, want), (rank, step, got)
+    dist.barrier()
+    if rank == 1:
+        time.sleep(4)  # never posts the next step
+        status = "skipped"
+    else:
+        try:
+            ex(torch.zeros(5, dtype=torch.int64))
+            status = "returned"
+        except RuntimeError as exc:
+            status = "raised " + str(exc)
+    with open(os.path.join(outdir, f"rank{rank}.txt"), "w") as f:
+        f.write(status)
+    dist.barrier()
+    ex.close()
+    dist.destroy_process_group()
+
+
+def test_shared_memory_count_exchange_and_its_timeout():
+    with tempfile.TemporaryDirectory() as d:
+        mp.spawn(_shm_worker, args=(2, _free_port(), d), nprocs=2, join=True)
+        status = open(os.path.join(d, "rank0.txt")).read()
+        assert status.startswith("raised") and "did not post" in status, status
