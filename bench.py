@@ -52,6 +52,9 @@ def parse():
     ap.add_argument("--max-experts", type=int, default=None,
                     help="keep only the first K experts (and their rows): a smaller case of the "
                          "same workload for ncu captures")
+    ap.add_argument("--ffn", action="store_true",
+                    help="time the MoE expert FFN (fused SwiGLU gate/up GEMM + down GEMM) on the "
+                         "config's routing instead of the single grouped GEMM")
     ap.add_argument("--kernel-only", action="store_true",
                     help="warm-up + timed launches only (no e2e / CPU baseline / clocks): the "
                          "command profiled with ncu")
@@ -370,8 +373,74 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_ffn(args):
+    """MoE expert FFN forward: SwiGLU(A @ W1) @ W2 over the config's expert segments."""
+    import torch
+    import torch.nn.functional as F
+    from gmm_b200 import hopper_gmm_fwd, moe_ffn
+    from gmm_b200.configs import CONFIGS, batch_sizes_for
+    cid = args.config or 2
+    cfg = CONFIGS[cid]
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    bs = batch_sizes_for(cfg)
+    E, dim = cfg.num_experts, cfg.dim
+    inter = cfg.dim_out // 2 if cid == 3 else cfg.dim_out  # cfg3's dim_out is already gate+up
+    g = torch.Generator(device=dev).manual_seed(cfg.seed)
+    a = torch.randn(cfg.rows, dim, generator=g, device=dev).to(cfg.dtype)
+    tb = cfg.trans_b
+    w1 = torch.empty(*((E, 2 * inter, dim) if tb else (E, dim, 2 * inter)), dtype=cfg.dtype, device=dev)
+    w2 = torch.empty(*((E, dim, inter) if tb else (E, inter, dim)), dtype=cfg.dtype, device=dev)
+    for e in range(E):
+        w1[e].copy_(torch.randn(w1.shape[1:], generator=g, device=dev) / math.sqrt(dim))
+        w2[e].copy_(torch.randn(w2.shape[1:], generator=g, device=dev) / math.sqrt(inter))
+    flops = 2.0 * cfg.rows * dim * 2 * inter + 2.0 * cfg.rows * inter * dim
+
+    def fused():
+        return moe_ffn(a, w1, w2, bs, tb, tb)
+
+    def unfused():  # two plain grouped GEMMs with the activation as separate torch ops
+        gu = hopper_gmm_fwd(a, w1, bs, tb)
+        h = F.silu(gu[:, :inter]) * gu[:, inter:]
+        return hopper_gmm_fwd(h, w2, bs, tb)
+
+    def timed(fn, steps):
+        for _ in range(max(3, args.warmup)):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+    steps = max(1, min(args.steps, 50))
+    ms = timed(fused, steps)
+    ms_unfused = timed(unfused, steps)
+    peaks, src = load_peaks()
+    value = flops / (ms * 1e-3) / 1e12
+    print(json.dumps({
+        "metric": "MoE expert FFN forward TFLOP/s (SwiGLU gate/up grouped GEMM + down grouped GEMM)",
+        "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": 1, "steps": steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "dtype": {torch.bfloat16: "bf16", torch.float16: "fp16"}[cfg.dtype], "data": "synthetic",
+        "config": {"workload": f"cfg{cid} routing, expert FFN", "experts": E, "dim": dim,
+                   "inter": inter, "rows": cfg.rows, "trans_b": tb},
+        "unfused_ms_per_step": round(ms_unfused, 4),
+        "unfused_value": round(flops / (ms_unfused * 1e-3) / 1e12, 2),
+        "roofline": {"bound": "tensor", "achieved": round(value, 2), "peak": peaks["bf16_tflops"],
+                     "unit": "TFLOP/s", "frac": round(value / peaks["bf16_tflops"], 4),
+                     "peak_source": f"{src} (burst)"},
+        "gpu_launches": 2 * steps}), flush=True)
+
+
 def main():
     args = parse()
+    if args.ffn and args.impl == "ours":
+        run_ffn(args)
+        return
     if args.impl == "reference":
         run_reference(args)
         return

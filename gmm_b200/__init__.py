@@ -77,6 +77,44 @@ if _HAS_C:
         n = b.shape[1] if trans_b else b.shape[2]
         return torch.empty(num_tokens, n, dtype=a.dtype, device=a.device)
 
+    def _gmm_swiglu_fake(a, b, batch_sizes, trans_b):
+        n = b.shape[1] if trans_b else b.shape[2]
+        return torch.empty(a.shape[0], n // 2, dtype=a.dtype, device=a.device)
+
+    try:  # absent only in a stale build; `python -m gmm_b200.build` refreshes it
+        torch.library.register_fake("hopper_gmm_fwd::gmm_swiglu")(_gmm_swiglu_fake)
+    except RuntimeError:
+        warnings.warn("gmm_b200._C predates gmm_swiglu; rebuild with `python -m gmm_b200.build`",
+                      RuntimeWarning)
+
+
+def gmm_swiglu(a: torch.Tensor, b: torch.Tensor, batch_sizes: torch.Tensor,
+               trans_b: bool = False) -> torch.Tensor:
+    """Fused MoE gate/up projection: ``silu(a @ gate[e]) * (a @ up[e])`` per expert segment.
+
+    ``b`` holds each expert's gate and up projections side by side:
+    ``[E, dim, 2*I]`` with columns ``[gate | up]`` (``trans_b=False``) or
+    ``[E, 2*I, dim]`` with rows ``[gate | up]`` (``trans_b=True``).  Returns
+    ``[num_tokens, I]``; the activation is applied to the fp32 accumulators
+    inside the GEMM epilogue (bf16 / fp16).
+    """
+    if not _HAS_C:
+        raise RuntimeError("gmm_b200._C is not available. Build with `python -m gmm_b200.build`.")
+    return torch.ops.hopper_gmm_fwd.gmm_swiglu(a, b, batch_sizes, trans_b)
+
+
+def moe_ffn(a: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.Tensor,
+            batch_sizes: torch.Tensor, trans_gate_up: bool = False,
+            trans_down: bool = False) -> torch.Tensor:
+    """MoE expert FFN forward on expert-grouped rows: SwiGLU(a @ w_gate_up) @ w_down.
+
+    Two grouped GEMMs over the same ``batch_sizes``: the gate/up projection
+    with SiLU-and-multiply fused into its epilogue, then the down projection
+    (``w_down`` is ``[E, I, dim]``, or ``[E, dim, I]`` with ``trans_down``).
+    """
+    h = gmm_swiglu(a, w_gate_up, batch_sizes, trans_gate_up)
+    return hopper_gmm_fwd(h, w_down, batch_sizes, trans_down)
+
 
 def hopper_gmm_fwd_host(a, b, batch_sizes, trans_b=False, out=None, device=None):
     """``hopper_gmm_fwd`` on host-resident (pinned) operands, with the transfers pipelined

@@ -113,7 +113,9 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_pair_kernel(const __grid_cons
       for (int tile = pair; ok && tile < p.total_tiles; tile += num_pairs) {
         const Tile t = decode_tile<C::BM, C::BN>(tv, n_tiles, tile, g);
         const int arow = t.row0 + C::BM_CTA * static_cast<int>(cta);
-        const int bcol = t.n0 + C::BN_CTA * static_cast<int>(cta);
+        // SwiGLU: the leader holds the tile's 128 gate columns, the peer the matching up columns.
+        const int bcol = !p.act ? t.n0 + C::BN_CTA * static_cast<int>(cta)
+                                : (t.n0 >> 1) + (cta ? p.act_cols : 0);
         for (int kb = 0; kb < k_blocks; ++kb) {
           if (!mbar_wait(smem_u32(empty_bar + stage), phase ^ 1, abort_flag)) {
             ok = false;
@@ -201,8 +203,12 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_pair_kernel(const __grid_cons
       const int row0 = t.row0 + C::BM_CTA * static_cast<int>(cta);
       if (quarter * 32 < rows_cta) {  // warp-uniform
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * C::BN;
-        drain_slab<OutT, C::BN>(p, tv, g, row0 + quarter * 32, min(32, rows_cta - quarter * 32), t.n0,
-                                taddr, stage, lane);
+        if (p.act)
+          drain_slab_swiglu<OutT>(p, tv, g, row0 + quarter * 32, min(32, rows_cta - quarter * 32),
+                                  t.n0 >> 1, taddr, stage, lane);
+        else
+          drain_slab<OutT, C::BN>(p, tv, g, row0 + quarter * 32, min(32, rows_cta - quarter * 32), t.n0,
+                                  taddr, stage, lane);
       }
       tc_fence_before();
       __syncwarp();

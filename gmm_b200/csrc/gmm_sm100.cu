@@ -64,7 +64,8 @@ struct __align__(64) GmmParams {
   int dim_out;
   int remote;  // 1: output rows go to the ranks they came from (expert-parallel combine)
   int world;   // ranks addressed through d_peer (remote mode)
-  int pad_;
+  int act;     // 1: SwiGLU -- B is [gate | up] (act_cols columns each); D = silu(gate) * up
+  int act_cols;
   void* d_peer[kMaxPeers];  // each rank's output buffer (remote mode)
   // Table of the non-empty groups, laid out as
   //   row_off[G+1] | tile_off[G+1] | expert[G] [| src_off[G][W+1] | dst_row[G][W]]
@@ -244,6 +245,59 @@ __device__ __forceinline__ void drain_slab(const GmmParams& p, const TableView& 
   }
 }
 
+__device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + __expf(-g)) * u; }
+
+// SwiGLU variant of drain_slab: TMEM columns [0, 128) hold the tile's gate
+// projections and [128, 256) the matching up projections; writes
+// silu(gate) * up (fp32) rounded to the output type, 128 columns per tile.
+template <typename OutT>
+__device__ __forceinline__ void drain_slab_swiglu(const GmmParams& p, const TableView& tv, int g,
+                                                  int slab_row0, int slab_rows, int n0, uint32_t taddr,
+                                                  uint32_t stage, int lane) {
+  static_assert(sizeof(OutT) == 2, "SwiGLU epilogue is 16-bit");
+  OutT* rp[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int rr = i * 4 + (lane >> 3);
+    rp[i] = rr < slab_rows ? out_row<OutT>(p, tv, g, slab_row0 + rr) : nullptr;
+  }
+  const int ch = lane & 7;
+  const uint32_t my_row = stage + lane * 128;
+#pragma unroll 1
+  for (int c0 = 0; c0 < 128; c0 += 64) {
+    const int col = n0 + c0;
+    if (col >= p.dim_out) break;  // warp-uniform
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint32_t gv[32], uv[32];
+      tmem_ld_32x32b_x32(taddr + c0 + h * 32, gv);
+      tmem_ld_32x32b_x32(taddr + 128 + c0 + h * 32, uv);
+      tmem_wait_ld();
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float a[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          a[j] = silu_mul(__uint_as_float(gv[8 * q + j]), __uint_as_float(uv[8 * q + j]));
+        uint4 pk;
+        pk.x = pack2<OutT>(a[0], a[1]);
+        pk.y = pack2<OutT>(a[2], a[3]);
+        pk.z = pack2<OutT>(a[4], a[5]);
+        pk.w = pack2<OutT>(a[6], a[7]);
+        st_shared_v4(my_row + (((h * 4 + q) ^ (lane & 7)) << 4), pk);
+      }
+    }
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int rr = i * 4 + (lane >> 3);
+      const uint4 val = ld_shared_v4(stage + rr * 128 + ((ch ^ (rr & 7)) << 4));
+      if (rp[i] && col + ch * 8 < p.dim_out) *reinterpret_cast<uint4*>(rp[i] + col + ch * 8) = val;
+    }
+    __syncwarp();
+  }
+}
+
 template <int kKind, bool kBMnMajor>
 __global__ void __launch_bounds__(kThreads, 1) gmm_persistent_kernel(const __grid_constant__ GmmParams p) {
   using C = Cfg<kKind, kBMnMajor>;
@@ -324,11 +378,17 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_persistent_kernel(const __gri
             tma_load_3d(smem_u32(sb), &p.tmap_b, fb, k0, t.n0, t.expert);
             tma_load_3d(smem_u32(sb + C::kBBytes), &p.tmap_b2, fb, k0, t.n0, t.expert);
           } else if (kBMnMajor) {
-            // B[e] is [K, N] (N contiguous): BN/64 panels of [BK rows][64 cols].
+            // B[e] is [K, N] (N contiguous): BN/64 panels of [BK rows][64 cols];
+            // SwiGLU tiles take two gate panels and the two matching up panels.
 #pragma unroll
-            for (int c = 0; c < C::BN / 64; ++c)
-              tma_load_3d(smem_u32(sb + c * (C::BK * 128)), &p.tmap_b, fb, t.n0 + 64 * c, k0,
-                          t.expert);
+            for (int c = 0; c < C::BN / 64; ++c) {
+              const int col = !p.act ? t.n0 + 64 * c
+                                     : (c < 2 ? (t.n0 >> 1) + 64 * c : p.act_cols + (t.n0 >> 1) + 64 * (c - 2));
+              tma_load_3d(smem_u32(sb + c * (C::BK * 128)), &p.tmap_b, fb, col, k0, t.expert);
+            }
+          } else if (p.act) {  // K-major [gate rows | up rows], 128 each (box of 128 rows)
+            tma_load_3d(smem_u32(sb), &p.tmap_b, fb, k0, t.n0 >> 1, t.expert);
+            tma_load_3d(smem_u32(sb + 128 * 128), &p.tmap_b, fb, k0, p.act_cols + (t.n0 >> 1), t.expert);
           } else {
             tma_load_3d(smem_u32(sb), &p.tmap_b, fb, k0, t.n0, t.expert);
           }
@@ -414,8 +474,18 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_persistent_kernel(const __gri
       const Tile t = decode_tile<C::BM, C::BN>(tv, n_tiles, tile, g);
       if (quarter * 32 < t.rows) {  // warp-uniform: some row of this quarter is live
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * C::BN;
-        drain_slab<OutT, C::BN>(p, tv, g, t.row0 + quarter * 32, min(32, t.rows - quarter * 32), t.n0,
-                                taddr, stage, lane);
+        if constexpr (!C::kTf32) {
+          if (p.act) {
+            drain_slab_swiglu<OutT>(p, tv, g, t.row0 + quarter * 32, min(32, t.rows - quarter * 32),
+                                    t.n0 >> 1, taddr, stage, lane);
+          } else {
+            drain_slab<OutT, C::BN>(p, tv, g, t.row0 + quarter * 32, min(32, t.rows - quarter * 32),
+                                    t.n0, taddr, stage, lane);
+          }
+        } else {
+          drain_slab<OutT, C::BN>(p, tv, g, t.row0 + quarter * 32, min(32, t.rows - quarter * 32), t.n0,
+                                  taddr, stage, lane);
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -774,7 +844,8 @@ bool append_ep_table(Plan& pl, const int64_t* local_bs, int64_t E, const EpRoute
 
 int forward_impl(const void* A, const void* B, const int64_t* batch_sizes, int64_t num_experts,
                  int64_t num_tokens, int64_t dim, int64_t dim_out, int dtype, int trans_b, void* D,
-                 void* workspace, size_t workspace_bytes, void* stream_ptr, const EpRoute* ep) {
+                 void* workspace, size_t workspace_bytes, void* stream_ptr, const EpRoute* ep,
+                 int act = 0) {
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
   Plan pl;
   int rc = make_plan(batch_sizes, num_experts, num_tokens, dim, dim_out, dtype, pl);
@@ -786,6 +857,13 @@ int forward_impl(const void* A, const void* B, const int64_t* batch_sizes, int64
   const int64_t T = num_tokens, K = dim, N = dim_out, E = num_experts;
   if (T == 0 || N == 0) return GMM_OK;  // nothing to write
   const int es = elem_size(dtype);
+  // SwiGLU: B has 2*I output columns ([gate | up]); D has I = N / 2 columns.
+  const int64_t N_out = act ? N / 2 : N;
+  if (act) {
+    if (dtype == GMM_DTYPE_F32) return fail(GMM_ERR_DTYPE, "the fused SwiGLU path takes bf16 / fp16");
+    if (N % 16 != 0)
+      return fail(GMM_ERR_ALIGNMENT, "SwiGLU needs the gate/up width (dim_out / 2) to be a multiple of 8");
+  }
   if (ep) {
     if (ep->world < 1 || ep->world > kMaxPeers || !ep->out_peers)
       return fail(GMM_ERR_INVALID_ARGUMENT, "expert-parallel world must be 1.." + std::to_string(kMaxPeers));
@@ -806,8 +884,8 @@ int forward_impl(const void* A, const void* B, const int64_t* batch_sizes, int64
   if (ce != cudaSuccess) return cuda_fail(ce, "cudaGetDevice");
   DeviceInfo* di = nullptr;
   if ((rc = device_info(dev, &di)) != GMM_OK) return rc;
-  if (K == 0) {  // empty contraction: D = 0
-    ce = cudaMemsetAsync(D, 0, static_cast<size_t>(T) * N * es, stream);
+  if (K == 0) {  // empty contraction: D = 0 (SwiGLU: silu(0) * 0 = 0)
+    ce = cudaMemsetAsync(D, 0, static_cast<size_t>(T) * N_out * es, stream);
     return ce == cudaSuccess ? GMM_OK : cuda_fail(ce, "cudaMemsetAsync");
   }
   if (!A || !B) return fail(GMM_ERR_INVALID_ARGUMENT, "A or B is null");
@@ -824,12 +902,14 @@ int forward_impl(const void* A, const void* B, const int64_t* batch_sizes, int64
   GmmParams prm;
   std::memset(&prm, 0, sizeof(prm));
   prm.d = D;
-  prm.ldd = N;
+  prm.ldd = N_out;
   prm.num_groups = pl.num_groups;
   prm.n_tiles = pl.n_tiles;
   prm.k_blocks = pl.k_blocks;
   prm.total_tiles = pl.total_tiles;
-  prm.dim_out = static_cast<int>(N);
+  prm.dim_out = static_cast<int>(N_out);
+  prm.act = act;
+  prm.act_cols = act ? static_cast<int>(N_out) : 0;
   if (ep) {
     prm.remote = 1;
     prm.world = ep->world;
@@ -885,7 +965,7 @@ int forward_impl(const void* A, const void* B, const int64_t* batch_sizes, int64
     if ((rc = encode(&prm.tmap_a, tt, 2, A, adims, astr, abox))) return rc;
     if (trans_b) {  // B[e] is [N, K], K contiguous; a CTA of a pair holds half the tile's columns
       const cuuint64_t bdims[3] = {uK, uN, uE}, bstr[2] = {uK * 2, uN * uK * 2};
-      const cuuint32_t bbox[3] = {64, tile_rows == 256 ? 128u : 256u, 1};
+      const cuuint32_t bbox[3] = {64, (tile_rows == 256 || act) ? 128u : 256u, 1};
       if ((rc = encode(&prm.tmap_b, tt, 3, B, bdims, bstr, bbox))) return rc;
     } else {  // B[e] is [K, N], N contiguous
       const cuuint64_t bdims[3] = {uN, uK, uE}, bstr[2] = {uN * 2, uK * uN * 2};
@@ -1031,6 +1111,13 @@ int gmm_sm100_ep_gather(void* X, const void* const* src_peers, const int64_t* co
   ep_gather_kernel<<<std::max(blocks, 1), 256, 0, static_cast<cudaStream_t>(stream_ptr)>>>(prm);
   ce = cudaGetLastError();
   return ce == cudaSuccess ? GMM_OK : cuda_fail(ce, "ep gather launch");
+}
+
+int gmm_sm100_forward_swiglu(const void* A, const void* B, const int64_t* batch_sizes, int64_t num_experts,
+                             int64_t num_tokens, int64_t dim, int64_t dim_out, int dtype, int trans_b,
+                             void* D, void* workspace, size_t workspace_bytes, void* stream) {
+  return forward_impl(A, B, batch_sizes, num_experts, num_tokens, dim, dim_out, dtype, trans_b, D,
+                      workspace, workspace_bytes, stream, nullptr, 1);
 }
 
 int gmm_sm100_device_error(int* status_out, int clear) {

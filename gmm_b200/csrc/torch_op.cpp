@@ -71,10 +71,54 @@ at::Tensor hopper_gmm_forward(at::Tensor A, at::Tensor B, at::Tensor batch_sizes
   return D;
 }
 
+// Fused MoE gate/up projection + SwiGLU: B holds [gate | up] (2*I output
+// columns); returns silu(A @ Bgate) * (A @ Bup), [T, I].  No reference
+// counterpart (the reference's caller would run two GEMM segments with the
+// activation in between).
+at::Tensor gmm_swiglu(at::Tensor A, at::Tensor B, at::Tensor batch_sizes, bool transb) {
+  TORCH_CHECK(A.is_cuda() && A.is_contiguous(), "A must be a contiguous CUDA tensor");
+  TORCH_CHECK(B.is_cuda() && B.is_contiguous(), "B must be a contiguous CUDA tensor");
+  TORCH_CHECK(A.dim() == 2, "A must be 2D");
+  TORCH_CHECK(B.dim() == 3, "B must be 3D [num_experts, dim, 2*inter] (or [num_experts, 2*inter, dim])");
+  TORCH_CHECK(batch_sizes.is_cpu() && batch_sizes.dim() == 1 &&
+                  batch_sizes.scalar_type() == at::kLong,
+              "batch_sizes must be a 1D CPU int64 tensor");
+  TORCH_CHECK(A.scalar_type() == B.scalar_type(), "A and B must have the same dtype");
+  TORCH_CHECK(A.scalar_type() == at::kBFloat16 || A.scalar_type() == at::kHalf,
+              "gmm_swiglu supports bf16 / fp16");
+  const int device = A.get_device();
+  c10::cuda::CUDAGuard guard(device);
+  TORCH_CHECK(gmm_sm100_check_device(device) == GMM_OK, "gmm_swiglu: ", gmm_sm100_last_error());
+  const int64_t num_experts = batch_sizes.size(0);
+  const int64_t dim = A.size(1);
+  const int64_t dim_out = transb ? B.size(1) : B.size(2);
+  TORCH_CHECK(B.size(0) == num_experts, "B.size(0) must equal num_experts (batch_sizes.size(0))");
+  TORCH_CHECK((transb ? B.size(2) : B.size(1)) == dim, "B's contraction size must equal A.size(1) (dim)");
+  TORCH_CHECK(dim_out % 2 == 0, "B must hold gate and up projections of equal width");
+  const int dtype = A.scalar_type() == at::kBFloat16 ? GMM_DTYPE_BF16 : GMM_DTYPE_F16;
+  auto bs = batch_sizes.contiguous();
+  const int64_t* bs_ptr = bs.data_ptr<int64_t>();
+  at::Tensor D = at::empty({A.size(0), dim_out / 2}, A.options());
+  const size_t ws_bytes =
+      gmm_sm100_workspace_size(bs_ptr, num_experts, A.size(0), dim, dim_out, dtype, transb ? 1 : 0);
+  at::Tensor ws;
+  if (ws_bytes > 0) ws = at::empty({static_cast<int64_t>(ws_bytes)}, A.options().dtype(at::kByte));
+  cudaStream_t stream = c10::cuda::getCurrentCUDAStream(device).stream();
+  const int rc = gmm_sm100_forward_swiglu(A.data_ptr(), B.data_ptr(), bs_ptr, num_experts, A.size(0),
+                                          dim, dim_out, dtype, transb ? 1 : 0, D.data_ptr(),
+                                          ws_bytes ? ws.data_ptr() : nullptr, ws_bytes, stream);
+  TORCH_CHECK(rc == GMM_OK, gmm_sm100_last_error());
+  return D;
+}
+
 }  // namespace gmm_b200
 
 TORCH_LIBRARY(hopper_gmm_fwd, m) {
   m.def("gmm(Tensor A, Tensor B, Tensor batch_sizes, bool trans_b) -> Tensor");
+  m.def("gmm_swiglu(Tensor A, Tensor B, Tensor batch_sizes, bool trans_b) -> Tensor");
 }
 
-TORCH_LIBRARY_IMPL(hopper_gmm_fwd, CUDA, m) { m.impl("gmm", &gmm_b200::hopper_gmm_forward); }
+TORCH_LIBRARY_IMPL(hopper_gmm_fwd, CUDA, m) {
+  m.impl("gmm", &gmm_b200::hopper_gmm_forward);
+  m.impl("gmm_swiglu", &gmm_b200::gmm_swiglu);
+}

@@ -82,6 +82,20 @@ int gmm_sm100_forward(const void* A, const void* B, const int64_t* batch_sizes,
                       int dtype, int trans_b, void* D, void* workspace, size_t workspace_bytes,
                       void* stream);
 
+/* Fused MoE gate/up projection with SwiGLU.  No reference counterpart: the
+ * reference stops at the grouped GEMM, and its MoE layer would call it twice
+ * (gate+up, then down) with the activation in between.  B holds each
+ * expert's gate and up projections side by side -- [E, dim, 2*I] with
+ * columns [gate | up] (trans_b = 0) or [E, 2*I, dim] with rows [gate | up]
+ * (trans_b = 1); dim_out = 2*I, a multiple of 16.  D is [num_tokens, I]:
+ *   D[rows_e] = silu(A[rows_e] @ Bgate[e]) * (A[rows_e] @ Bup[e])
+ * computed from the fp32 accumulators and rounded once; bf16 / fp16 only.
+ * Workspace as gmm_sm100_forward. */
+int gmm_sm100_forward_swiglu(const void* A, const void* B, const int64_t* batch_sizes,
+                             int64_t num_experts, int64_t num_tokens, int64_t dim, int64_t dim_out,
+                             int dtype, int trans_b, void* D, void* workspace,
+                             size_t workspace_bytes, void* stream);
+
 /* Reads (and with clear != 0, resets) the device-side error word of the
  * current device: 0, or a gmm_status recorded by a kernel whose bounded wait
  * ran out.  Synchronises the device.  No reference counterpart (the

@@ -111,6 +111,17 @@ def gmm_oracle_np(a, b, batch_sizes, trans_b: bool = False) -> np.ndarray:
     return out
 
 
+def swiglu_oracle(a, b, batch_sizes, trans_b: bool = False) -> np.ndarray:
+    """silu(gate) * up of the fp64 grouped GEMM, B holding [gate | up] (float64).
+
+    The MoE FFN's activation (SiLU(x) = x / (1 + exp(-x))) applied to the
+    reference per-expert matmul; no reference counterpart of its own."""
+    acc = gmm_oracle_c(a, b, batch_sizes, trans_b)
+    half = acc.shape[1] // 2
+    g, u = acc[:, :half], acc[:, half:]
+    return g / (1.0 + np.exp(-g)) * u
+
+
 def ref_gmm_port(a, b, batch_sizes, trans_b: bool = False):
     """The reference's ``ref_gmm`` (tests/test_forward.py:8-15) on torch CPU tensors.
 

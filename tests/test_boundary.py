@@ -96,3 +96,15 @@ def test_cabi_errstr_and_workspace():
     # more than 1024 non-empty experts: the table moves to the workspace
     ws = capi.workspace_size([1] * 2000, 2000, 64, 64, capi.GMM_DTYPE_F16, True)
     assert ws == ((3 * 2000 + 2) * 4 + 255) // 256 * 256
+
+
+def test_swiglu_op_schema_and_fake():
+    import gmm_b200  # noqa: F401
+    from torch._subclasses.fake_tensor import FakeTensorMode
+    assert str(torch.ops.hopper_gmm_fwd.gmm_swiglu.default._schema) == (
+        "hopper_gmm_fwd::gmm_swiglu(Tensor A, Tensor B, Tensor batch_sizes, bool trans_b) -> Tensor")
+    with FakeTensorMode():
+        a = torch.empty(64, 32, dtype=torch.bfloat16, device="cuda")
+        b = torch.empty(2, 32, 96, dtype=torch.bfloat16, device="cuda")
+        out = gmm_b200.gmm_swiglu(a, b, torch.tensor([30, 34]))
+        assert tuple(out.shape) == (64, 48)
