@@ -34,6 +34,26 @@ _SIGNATURES = {
                                                 ctypes.c_int64, ctypes.c_int, ctypes.c_int,
                                                 ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
                                                 ctypes.c_void_p]),
+    "gmm_sm100_forward_dev": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                             ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                             ctypes.c_int64, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                             ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
+                                             ctypes.c_void_p]),
+    "gmm_sm100_dev_workspace_size": (ctypes.c_size_t, [ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                                       ctypes.c_int64, ctypes.c_int]),
+    "gmm_sm100_moe_topk": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_int,
+                                          ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
+                                          ctypes.c_void_p]),
+    "gmm_sm100_moe_permute": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                                             ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
+                                             ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                             ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
+                                             ctypes.c_void_p]),
+    "gmm_sm100_moe_permute_workspace_size": (ctypes.c_size_t, [ctypes.c_int64, ctypes.c_int]),
+    "gmm_sm100_moe_unpermute": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                               ctypes.c_int64, ctypes.c_int, ctypes.c_int64,
+                                               ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]),
+    "gmm_sm100_moe_last_error": (ctypes.c_char_p, []),
     "gmm_sm100_ep_gather": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                            ctypes.c_void_p, ctypes.c_int64, ctypes.c_int,
                                            ctypes.c_int64, ctypes.c_void_p]),

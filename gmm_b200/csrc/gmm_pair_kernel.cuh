@@ -36,7 +36,7 @@ struct PairCfg {
   static constexpr int kTmemCols = 2 * BN;
   static constexpr uint32_t kIdesc = make_idesc(kKind == kKindBf16 ? 1u : 0u, kBMnMajor, BM, BN);
   static constexpr int kBarBytes = 256;
-  static constexpr int kSmemBytes = kStages * kStageBytes + kBarBytes + kEpiStageBytes + 1024;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kBarBytes + kEpiStageBytes + kDevTableBytes + 1024;
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
 
@@ -96,9 +96,20 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_pair_kernel(const __grid_cons
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const TableView tv = make_table_view(p);
   const int n_tiles = p.n_tiles;
   const int k_blocks = p.k_blocks;
+  int num_groups = p.num_groups, total_tiles = p.total_tiles;
+  const int32_t* tab = p.ext_table ? p.ext_table : p.inline_table;
+  if (p.dev_bs) {  // both CTAs of a pair build the same table
+    int32_t* dtab = reinterpret_cast<int32_t*>(epi_stage + kEpiStageBytes);
+    int32_t* meta = dtab + 3 * kMaxDevExperts + 2;
+    build_device_table(p, dtab, meta, reinterpret_cast<int*>(meta + 3));
+    num_groups = meta[0];
+    total_tiles = meta[1] * n_tiles;
+    if (threadIdx.x == 0 && leader && meta[2] != 0) atomicCAS(&g_device_error, 0, meta[2]);
+    tab = dtab;
+  }
+  const TableView tv = make_table_view(p, tab, num_groups);
   const int pair = blockIdx.x >> 1;
   const int num_pairs = gridDim.x >> 1;
   bool aborted_here = false;
@@ -110,7 +121,7 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_pair_kernel(const __grid_cons
       uint32_t phase = 0;
       bool ok = true;
       int g = 0;
-      for (int tile = pair; ok && tile < p.total_tiles; tile += num_pairs) {
+      for (int tile = pair; ok && tile < total_tiles; tile += num_pairs) {
         const Tile t = decode_tile<C::BM, C::BN>(tv, n_tiles, tile, g);
         const int arow = t.row0 + C::BM_CTA * static_cast<int>(cta);
         // SwiGLU: the leader holds the tile's 128 gate columns, the peer the matching up columns.
@@ -151,7 +162,7 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_pair_kernel(const __grid_cons
       uint32_t phase = 0;
       bool ok = true;
       int local = 0;
-      for (int tile = pair; ok && tile < p.total_tiles; tile += num_pairs, ++local) {
+      for (int tile = pair; ok && tile < total_tiles; tile += num_pairs, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait(smem_u32(tempty_bar + acc), acc_phase ^ 1, abort_flag)) break;
@@ -193,7 +204,7 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_pair_kernel(const __grid_cons
     const uint32_t tempty_leader0 = map_shared_to_rank(smem_u32(tempty_bar), 0);
     int g = 0;
     int local = 0;
-    for (int tile = pair; tile < p.total_tiles; tile += num_pairs, ++local) {
+    for (int tile = pair; tile < total_tiles; tile += num_pairs, ++local) {
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(smem_u32(tfull_bar + acc), acc_phase, abort_flag)) break;

@@ -45,6 +45,8 @@ __device__ int g_device_error = 0;
 constexpr int kInlineGroups = 1024;  // groups whose table travels in the kernel parameters
 constexpr int kInlineTableInts = 3 * kInlineGroups + 2;
 constexpr int kMaxPeers = 8;         // expert-parallel ranks a kernel can address
+constexpr int kMaxDevExperts = 1024;  // experts a device-built table can hold
+constexpr int kDevTableBytes = (3 * kMaxDevExperts + 64) * 4;  // row_off | tile_off | expert | meta | scan scratch
 constexpr int kMBlock = 16;          // m-tiles per raster block (L2 reuse of B columns)
 constexpr int kThreads = 256;        // 8 warps: TMA, MMA, TMEM alloc, idle, 4x epilogue
 constexpr int kEpiStageBytes = 4 * 32 * 128;  // epilogue staging: 4 warps x 32 rows x 128 B
@@ -66,6 +68,15 @@ struct __align__(64) GmmParams {
   int world;   // ranks addressed through d_peer (remote mode)
   int act;     // 1: SwiGLU -- B is [gate | up] (act_cols columns each); D = silu(gate) * up
   int act_cols;
+  // Device-resident batch sizes (dev_bs != nullptr): every CTA builds the
+  // group table in shared memory from dev_bs[0..dev_experts) (int32); rows
+  // past rows_cap are never touched and a bad table is reported through the
+  // device error word.
+  const int32_t* dev_bs;
+  int dev_experts;
+  int rows_cap;
+  int tile_rows;  // 128 or 256 (m-tile height the device table is built for)
+  int pad2_;
   void* d_peer[kMaxPeers];  // each rank's output buffer (remote mode)
   // Table of the non-empty groups, laid out as
   //   row_off[G+1] | tile_off[G+1] | expert[G] [| src_off[G][W+1] | dst_row[G][W]]
@@ -97,7 +108,7 @@ struct Cfg {
   static constexpr uint32_t kIdesc =
       make_idesc(kTf32 ? 2u : (kKind == kKindBf16 ? 1u : 0u), kBMnMajor, BM, BN);
   static constexpr int kBarBytes = 256;
-  static constexpr int kSmemBytes = kStages * kStageBytes + kBarBytes + kEpiStageBytes + 1024;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kBarBytes + kEpiStageBytes + kDevTableBytes + 1024;
   static_assert(!(kTf32 && kBMnMajor), "fp32 B is staged K-major by the split pre-pass");
   static_assert(kABytes % 1024 == 0 && kBBytes % 1024 == 0, "swizzle atoms need 1 KB alignment");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
@@ -111,15 +122,101 @@ struct TableView {
   const int32_t* dst_row;  // remote mode
 };
 
-__device__ __forceinline__ TableView make_table_view(const GmmParams& p) {
-  const int32_t* tab = p.ext_table ? p.ext_table : p.inline_table;
+__device__ __forceinline__ TableView make_table_view(const GmmParams& p, const int32_t* tab,
+                                                     int num_groups) {
   TableView tv;
   tv.row_off = tab;
-  tv.tile_off = tab + p.num_groups + 1;
-  tv.expert = tab + 2 * (p.num_groups + 1);
-  tv.src_off = tv.expert + p.num_groups;
-  tv.dst_row = tv.src_off + p.num_groups * (p.world + 1);
+  tv.tile_off = tab + num_groups + 1;
+  tv.expert = tab + 2 * (num_groups + 1);
+  tv.src_off = tv.expert + num_groups;
+  tv.dst_row = tv.src_off + num_groups * (p.world + 1);
   return tv;
+}
+
+// Exclusive block scan (256 threads) of three per-thread values; returns the
+// block totals.  `scratch` holds 8 warps x 3 ints.
+__device__ __forceinline__ void block_scan3(int (&v)[3], int (&tot)[3], int* scratch) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl[3] = {v[0], v[1], v[2]};
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      const int o = __shfl_up_sync(0xffffffffu, incl[j], d);
+      if (lane >= d) incl[j] += o;
+    }
+  }
+  if (lane == 31)
+    for (int j = 0; j < 3; ++j) scratch[warp * 3 + j] = incl[j];
+  __syncthreads();
+  int warp_off[3] = {0, 0, 0};
+  for (int j = 0; j < 3; ++j) {
+    tot[j] = 0;
+    for (int w = 0; w < 8; ++w) {
+      if (w < warp) warp_off[j] += scratch[w * 3 + j];
+      tot[j] += scratch[w * 3 + j];
+    }
+  }
+  for (int j = 0; j < 3; ++j) v[j] = incl[j] - v[j] + warp_off[j];
+  __syncthreads();
+}
+
+// Build the group table from device batch sizes into shared memory (all 256
+// threads).  Layout as the host table: row_off[G+1] | tile_off[G+1] |
+// expert[G]; meta[0] = G, meta[1] = m-tiles, meta[2] = error status.
+__device__ void build_device_table(const GmmParams& p, int32_t* tab, int32_t* meta, int* scratch) {
+  const int E = p.dev_experts;
+  const int BM = p.tile_rows;
+  constexpr int kPer = kMaxDevExperts / kThreads;  // experts per thread (4)
+  int bsv[kPer];
+  int loc[3] = {0, 0, 0};  // rows, non-empty experts, m-tiles of this thread's experts
+  bool bad = false;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int e = threadIdx.x * kPer + i;
+    const int m = e < E ? p.dev_bs[e] : 0;
+    bad |= m < 0;
+    bsv[i] = m > 0 ? m : 0;
+    loc[0] += bsv[i];
+    loc[1] += bsv[i] > 0;
+    loc[2] += (bsv[i] + BM - 1) / BM;
+  }
+  int tot[3];
+  int pre[3] = {loc[0], loc[1], loc[2]};
+  block_scan3(pre, tot, scratch);
+  const int bad_any = __syncthreads_or(bad);
+  const int G = tot[1];
+  if (bad_any || tot[0] > p.rows_cap) {
+    if (threadIdx.x == 0) {
+      meta[0] = 0;
+      meta[1] = 0;
+      meta[2] = bad_any ? GMM_ERR_INVALID_ARGUMENT : GMM_ERR_BATCH_SUM;
+      tab[0] = 0;
+      tab[1] = 0;
+    }
+    __syncthreads();
+    return;
+  }
+  int row = pre[0], g = pre[1], mt = pre[2];
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    if (bsv[i] > 0) {
+      tab[g] = row;
+      tab[G + 1 + g] = mt;
+      tab[2 * (G + 1) + g] = threadIdx.x * kPer + i;
+      ++g;
+      mt += (bsv[i] + BM - 1) / BM;
+    }
+    row += bsv[i];
+  }
+  if (threadIdx.x == 0) {
+    tab[G] = tot[0];
+    tab[2 * G + 1] = tot[2];
+    meta[0] = G;
+    meta[1] = tot[2];
+    meta[2] = 0;
+  }
+  __syncthreads();
 }
 
 // Where output row `row` (a row of A, inside group g) is stored: D itself, or
@@ -347,9 +444,20 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_persistent_kernel(const __gri
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const TableView tv = make_table_view(p);
   const int n_tiles = p.n_tiles;
   const int k_blocks = p.k_blocks;
+  int num_groups = p.num_groups, total_tiles = p.total_tiles;
+  const int32_t* tab = p.ext_table ? p.ext_table : p.inline_table;
+  if (p.dev_bs) {
+    int32_t* dtab = reinterpret_cast<int32_t*>(epi_stage + kEpiStageBytes);
+    int32_t* meta = dtab + 3 * kMaxDevExperts + 2;
+    build_device_table(p, dtab, meta, reinterpret_cast<int*>(meta + 3));
+    num_groups = meta[0];
+    total_tiles = meta[1] * n_tiles;
+    if (threadIdx.x == 0 && meta[2] != 0) atomicCAS(&g_device_error, 0, meta[2]);
+    tab = dtab;
+  }
+  const TableView tv = make_table_view(p, tab, num_groups);
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -360,7 +468,7 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_persistent_kernel(const __gri
       for (int s = 0; s < C::kStages; ++s) issued[s] = 0;
       bool ok = true;
       int g = 0;
-      for (int tile = blockIdx.x; ok && tile < p.total_tiles; tile += gridDim.x) {
+      for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
         const Tile t = decode_tile<C::BM, C::BN>(tv, n_tiles, tile, g);
         for (int kb = 0; kb < k_blocks; ++kb) {
           if (!mbar_wait(smem_u32(empty_bar + stage), phase ^ 1, abort_flag)) {
@@ -412,7 +520,7 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_persistent_kernel(const __gri
       uint32_t phase = 0;
       bool ok = true;
       int local = 0;
-      for (int tile = blockIdx.x; ok && tile < p.total_tiles; tile += gridDim.x, ++local) {
+      for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait(smem_u32(tempty_bar + acc), acc_phase ^ 1, abort_flag)) break;
@@ -466,7 +574,7 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_persistent_kernel(const __gri
     const uint32_t stage = smem_u32(epi_stage) + quarter * (32 * 128);
     int g = 0;
     int local = 0;
-    for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, ++local) {
+    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++local) {
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(smem_u32(tfull_bar + acc), acc_phase, abort_flag)) break;
@@ -842,6 +950,82 @@ bool append_ep_table(Plan& pl, const int64_t* local_bs, int64_t E, const EpRoute
   return true;
 }
 
+// Operand preparation (fp32 hi/lo split pre-pass, tensor maps) and the
+// launch of the chosen kernel variant.  `grid_tiles` caps the grid (the tile
+// count when the host knows it).
+int setup_and_launch(GmmParams& prm, const void* A, const void* B, uint8_t* ws, size_t a_part,
+                     size_t b_part, int64_t T, int64_t K, int64_t N, int64_t E, int dtype, int trans_b,
+                     int64_t tile_rows, int act, int grid_tiles, DeviceInfo* di, cudaStream_t stream) {
+  int rc = GMM_OK;
+  cudaError_t ce;
+  struct {
+    size_t a_part, b_part, split_bytes;
+    int total_tiles;
+  } pl{a_part, b_part, 2 * a_part + 2 * b_part, grid_tiles};
+  const cuuint64_t uT = T, uK = K, uN = N, uE = E;
+  if (dtype == GMM_DTYPE_F32) {
+    float* a_hi = reinterpret_cast<float*>(ws);
+    float* a_lo = reinterpret_cast<float*>(ws + pl.a_part);
+    float* b_hi = reinterpret_cast<float*>(ws + 2 * pl.a_part);
+    float* b_lo = reinterpret_cast<float*>(ws + 2 * pl.a_part + pl.b_part);
+    const long long n4a = T * K / 4;
+    const int sgrid = static_cast<int>(std::min<long long>((n4a + 255) / 256, 4LL * di->sm_count));
+    split_tf32_kernel<<<std::max(sgrid, 1), 256, 0, stream>>>(
+        reinterpret_cast<const float4*>(A), reinterpret_cast<float4*>(a_hi), reinterpret_cast<float4*>(a_lo), n4a);
+    if (trans_b) {
+      const long long n4b = E * K * N / 4;
+      const int bgrid = static_cast<int>(std::min<long long>((n4b + 255) / 256, 4LL * di->sm_count));
+      split_tf32_kernel<<<std::max(bgrid, 1), 256, 0, stream>>>(
+          reinterpret_cast<const float4*>(B), reinterpret_cast<float4*>(b_hi), reinterpret_cast<float4*>(b_lo), n4b);
+    } else {
+      dim3 tg(static_cast<unsigned>((N + 31) / 32), static_cast<unsigned>((K + 31) / 32), static_cast<unsigned>(E));
+      split_tf32_transpose_kernel<<<tg, dim3(32, 8), 0, stream>>>(static_cast<const float*>(B), b_hi, b_lo,
+                                                                  static_cast<int>(K), static_cast<int>(N));
+    }
+    ce = cudaGetLastError();
+    if (ce != cudaSuccess) return cuda_fail(ce, "split pre-pass launch");
+    const cuuint64_t adims[2] = {uK, uT}, astr[1] = {uK * 4};
+    const cuuint32_t abox[2] = {32, 128};
+    const cuuint64_t bdims[3] = {uK, uN, uE}, bstr[2] = {uK * 4, uN * uK * 4};
+    const cuuint32_t bbox[3] = {32, 128, 1};
+    if ((rc = encode(&prm.tmap_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a_hi, adims, astr, abox)) ||
+        (rc = encode(&prm.tmap_a2, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a_lo, adims, astr, abox)) ||
+        (rc = encode(&prm.tmap_b, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, b_hi, bdims, bstr, bbox)) ||
+        (rc = encode(&prm.tmap_b2, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, b_lo, bdims, bstr, bbox)))
+      return rc;
+  } else {
+    const CUtensorMapDataType tt =
+        dtype == GMM_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const cuuint64_t adims[2] = {uK, uT}, astr[1] = {uK * 2};
+    const cuuint32_t abox[2] = {64, 128};
+    if ((rc = encode(&prm.tmap_a, tt, 2, A, adims, astr, abox))) return rc;
+    if (trans_b) {  // B[e] is [N, K], K contiguous; a CTA of a pair holds half the tile's columns
+      const cuuint64_t bdims[3] = {uK, uN, uE}, bstr[2] = {uK * 2, uN * uK * 2};
+      const cuuint32_t bbox[3] = {64, (tile_rows == 256 || act) ? 128u : 256u, 1};
+      if ((rc = encode(&prm.tmap_b, tt, 3, B, bdims, bstr, bbox))) return rc;
+    } else {  // B[e] is [K, N], N contiguous
+      const cuuint64_t bdims[3] = {uN, uK, uE}, bstr[2] = {uN * 2, uK * uN * 2};
+      const cuuint32_t bbox[3] = {64, 64, 1};
+      if ((rc = encode(&prm.tmap_b, tt, 3, B, bdims, bstr, bbox))) return rc;
+    }
+  }
+
+  const int grid = std::max(1, std::min(pl.total_tiles, di->sm_count));
+  if (dtype == GMM_DTYPE_F32) return launch_variant<kKindTf32x3, false>(prm, grid, stream, di, 0);
+  if (tile_rows == 256) {
+    if (dtype == GMM_DTYPE_BF16)
+      return trans_b ? launch_pair<kKindBf16, false>(prm, pl.total_tiles, stream, di, 5)
+                     : launch_pair<kKindBf16, true>(prm, pl.total_tiles, stream, di, 6);
+    return trans_b ? launch_pair<kKindF16, false>(prm, pl.total_tiles, stream, di, 7)
+                   : launch_pair<kKindF16, true>(prm, pl.total_tiles, stream, di, 8);
+  }
+  if (dtype == GMM_DTYPE_BF16)
+    return trans_b ? launch_variant<kKindBf16, false>(prm, grid, stream, di, 1)
+                   : launch_variant<kKindBf16, true>(prm, grid, stream, di, 2);
+  return trans_b ? launch_variant<kKindF16, false>(prm, grid, stream, di, 3)
+                 : launch_variant<kKindF16, true>(prm, grid, stream, di, 4);
+}
+
 int forward_impl(const void* A, const void* B, const int64_t* batch_sizes, int64_t num_experts,
                  int64_t num_tokens, int64_t dim, int64_t dim_out, int dtype, int trans_b, void* D,
                  void* workspace, size_t workspace_bytes, void* stream_ptr, const EpRoute* ep,
@@ -926,68 +1110,8 @@ int forward_impl(const void* A, const void* B, const int64_t* batch_sizes, int64
     prm.ext_table = reinterpret_cast<const int32_t*>(tdev);
   }
 
-  const cuuint64_t uT = T, uK = K, uN = N, uE = E;
-  if (dtype == GMM_DTYPE_F32) {
-    float* a_hi = reinterpret_cast<float*>(ws);
-    float* a_lo = reinterpret_cast<float*>(ws + pl.a_part);
-    float* b_hi = reinterpret_cast<float*>(ws + 2 * pl.a_part);
-    float* b_lo = reinterpret_cast<float*>(ws + 2 * pl.a_part + pl.b_part);
-    const long long n4a = T * K / 4;
-    const int sgrid = static_cast<int>(std::min<long long>((n4a + 255) / 256, 4LL * di->sm_count));
-    split_tf32_kernel<<<std::max(sgrid, 1), 256, 0, stream>>>(
-        reinterpret_cast<const float4*>(A), reinterpret_cast<float4*>(a_hi), reinterpret_cast<float4*>(a_lo), n4a);
-    if (trans_b) {
-      const long long n4b = E * K * N / 4;
-      const int bgrid = static_cast<int>(std::min<long long>((n4b + 255) / 256, 4LL * di->sm_count));
-      split_tf32_kernel<<<std::max(bgrid, 1), 256, 0, stream>>>(
-          reinterpret_cast<const float4*>(B), reinterpret_cast<float4*>(b_hi), reinterpret_cast<float4*>(b_lo), n4b);
-    } else {
-      dim3 tg(static_cast<unsigned>((N + 31) / 32), static_cast<unsigned>((K + 31) / 32), static_cast<unsigned>(E));
-      split_tf32_transpose_kernel<<<tg, dim3(32, 8), 0, stream>>>(static_cast<const float*>(B), b_hi, b_lo,
-                                                                  static_cast<int>(K), static_cast<int>(N));
-    }
-    ce = cudaGetLastError();
-    if (ce != cudaSuccess) return cuda_fail(ce, "split pre-pass launch");
-    const cuuint64_t adims[2] = {uK, uT}, astr[1] = {uK * 4};
-    const cuuint32_t abox[2] = {32, 128};
-    const cuuint64_t bdims[3] = {uK, uN, uE}, bstr[2] = {uK * 4, uN * uK * 4};
-    const cuuint32_t bbox[3] = {32, 128, 1};
-    if ((rc = encode(&prm.tmap_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a_hi, adims, astr, abox)) ||
-        (rc = encode(&prm.tmap_a2, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a_lo, adims, astr, abox)) ||
-        (rc = encode(&prm.tmap_b, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, b_hi, bdims, bstr, bbox)) ||
-        (rc = encode(&prm.tmap_b2, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, b_lo, bdims, bstr, bbox)))
-      return rc;
-  } else {
-    const CUtensorMapDataType tt =
-        dtype == GMM_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-    const cuuint64_t adims[2] = {uK, uT}, astr[1] = {uK * 2};
-    const cuuint32_t abox[2] = {64, 128};
-    if ((rc = encode(&prm.tmap_a, tt, 2, A, adims, astr, abox))) return rc;
-    if (trans_b) {  // B[e] is [N, K], K contiguous; a CTA of a pair holds half the tile's columns
-      const cuuint64_t bdims[3] = {uK, uN, uE}, bstr[2] = {uK * 2, uN * uK * 2};
-      const cuuint32_t bbox[3] = {64, (tile_rows == 256 || act) ? 128u : 256u, 1};
-      if ((rc = encode(&prm.tmap_b, tt, 3, B, bdims, bstr, bbox))) return rc;
-    } else {  // B[e] is [K, N], N contiguous
-      const cuuint64_t bdims[3] = {uN, uK, uE}, bstr[2] = {uN * 2, uK * uN * 2};
-      const cuuint32_t bbox[3] = {64, 64, 1};
-      if ((rc = encode(&prm.tmap_b, tt, 3, B, bdims, bstr, bbox))) return rc;
-    }
-  }
-
-  const int grid = std::max(1, std::min(pl.total_tiles, di->sm_count));
-  if (dtype == GMM_DTYPE_F32) return launch_variant<kKindTf32x3, false>(prm, grid, stream, di, 0);
-  if (tile_rows == 256) {
-    if (dtype == GMM_DTYPE_BF16)
-      return trans_b ? launch_pair<kKindBf16, false>(prm, pl.total_tiles, stream, di, 5)
-                     : launch_pair<kKindBf16, true>(prm, pl.total_tiles, stream, di, 6);
-    return trans_b ? launch_pair<kKindF16, false>(prm, pl.total_tiles, stream, di, 7)
-                   : launch_pair<kKindF16, true>(prm, pl.total_tiles, stream, di, 8);
-  }
-  if (dtype == GMM_DTYPE_BF16)
-    return trans_b ? launch_variant<kKindBf16, false>(prm, grid, stream, di, 1)
-                   : launch_variant<kKindBf16, true>(prm, grid, stream, di, 2);
-  return trans_b ? launch_variant<kKindF16, false>(prm, grid, stream, di, 3)
-                 : launch_variant<kKindF16, true>(prm, grid, stream, di, 4);
+  return setup_and_launch(prm, A, B, ws, pl.a_part, pl.b_part, T, K, N, E, dtype, trans_b, tile_rows, act,
+                          pl.total_tiles, di, stream);
 }
 
 }  // namespace
@@ -1118,6 +1242,77 @@ int gmm_sm100_forward_swiglu(const void* A, const void* B, const int64_t* batch_
                              void* D, void* workspace, size_t workspace_bytes, void* stream) {
   return forward_impl(A, B, batch_sizes, num_experts, num_tokens, dim, dim_out, dtype, trans_b, D,
                       workspace, workspace_bytes, stream, nullptr, 1);
+}
+
+size_t gmm_sm100_dev_workspace_size(int64_t num_experts, int64_t rows_cap, int64_t dim, int64_t dim_out,
+                                    int dtype) {
+  if (dtype != GMM_DTYPE_F32 || num_experts <= 0 || rows_cap <= 0) return 0;
+  return 2 * round_up(static_cast<size_t>(rows_cap) * dim * 4, 256) +
+         2 * round_up(static_cast<size_t>(num_experts) * dim * dim_out * 4, 256);
+}
+
+int gmm_sm100_forward_dev(const void* A, const void* B, const int32_t* batch_sizes_dev, int64_t num_experts,
+                          int64_t rows_cap, int64_t dim, int64_t dim_out, int dtype, int trans_b, int swiglu,
+                          void* D, void* workspace, size_t workspace_bytes, void* stream_ptr) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  if (num_experts < 1 || num_experts > kMaxDevExperts || rows_cap < 0 || dim < 0 || dim_out < 0)
+    return fail(GMM_ERR_INVALID_ARGUMENT, "device batch sizes need 1 <= num_experts <= 1024");
+  if (dtype != GMM_DTYPE_F32 && dtype != GMM_DTYPE_BF16 && dtype != GMM_DTYPE_F16)
+    return fail(GMM_ERR_DTYPE, "Unsupported dtype: only FP32 / BF16 / FP16 are supported");
+  if (swiglu && (dtype == GMM_DTYPE_F32 || dim_out % 16 != 0))
+    return fail(GMM_ERR_INVALID_ARGUMENT, "SwiGLU takes bf16 / fp16 and dim_out a multiple of 16");
+  if (rows_cap > INT32_MAX - 256 || dim > INT32_MAX || dim_out > INT32_MAX)
+    return fail(GMM_ERR_TOO_LARGE, "a dimension exceeds the int32 coordinate range");
+  const int64_t T = rows_cap, K = dim, N = dim_out, E = num_experts;
+  if (T == 0 || N == 0) return GMM_OK;
+  const int es = elem_size(dtype);
+  const int64_t N_out = swiglu ? N / 2 : N;
+  if (!D || !aligned16(D)) return fail(GMM_ERR_ALIGNMENT, "D must be non-null and 16-byte aligned");
+  if (!batch_sizes_dev || (reinterpret_cast<uintptr_t>(batch_sizes_dev) & 3u))
+    return fail(GMM_ERR_ALIGNMENT, "batch_sizes must be a 4-byte aligned device pointer");
+  if ((N * es) % 16 != 0) return fail(GMM_ERR_ALIGNMENT, "dim_out * element size must be a multiple of 16 bytes");
+  int dev = 0;
+  cudaError_t ce = cudaGetDevice(&dev);
+  if (ce != cudaSuccess) return cuda_fail(ce, "cudaGetDevice");
+  DeviceInfo* di = nullptr;
+  int rc = device_info(dev, &di);
+  if (rc != GMM_OK) return rc;
+  if (K == 0) {
+    ce = cudaMemsetAsync(D, 0, static_cast<size_t>(T) * N_out * es, stream);
+    return ce == cudaSuccess ? GMM_OK : cuda_fail(ce, "cudaMemsetAsync");
+  }
+  if (!A || !B || !aligned16(A) || !aligned16(B))
+    return fail(GMM_ERR_ALIGNMENT, "A and B must be non-null and 16-byte aligned");
+  if ((K * es) % 16 != 0) return fail(GMM_ERR_ALIGNMENT, "dim * element size must be a multiple of 16 bytes");
+  const size_t need = gmm_sm100_dev_workspace_size(E, T, K, N, dtype);
+  if (need > 0 && (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255u)))
+    return fail(GMM_ERR_WORKSPACE, "workspace needs " + std::to_string(need) + " bytes (256-byte aligned)");
+  // Tile rows from the capacity alone (the sizes are only known on the device).
+  int64_t tile_rows = 128;
+  if (dtype != GMM_DTYPE_F32) {
+    const char* force = std::getenv("GMM_SM100_TILE");
+    if (force && std::strcmp(force, "256") == 0) tile_rows = 256;
+    else if (!(force && std::strcmp(force, "128") == 0)) tile_rows = T >= 384 * E ? 256 : 128;
+  }
+  const int64_t BN = dtype == GMM_DTYPE_F32 ? 128 : 256;
+  const int64_t BK = dtype == GMM_DTYPE_F32 ? 32 : 64;
+  GmmParams prm;
+  std::memset(&prm, 0, sizeof(prm));
+  prm.d = D;
+  prm.ldd = N_out;
+  prm.n_tiles = static_cast<int>((N + BN - 1) / BN);
+  prm.k_blocks = static_cast<int>((K + BK - 1) / BK);
+  prm.dim_out = static_cast<int>(N_out);
+  prm.act = swiglu ? 1 : 0;
+  prm.act_cols = swiglu ? static_cast<int>(N_out) : 0;
+  prm.dev_bs = batch_sizes_dev;
+  prm.dev_experts = static_cast<int>(E);
+  prm.rows_cap = static_cast<int>(T);
+  prm.tile_rows = static_cast<int>(tile_rows);
+  const size_t a_part = dtype == GMM_DTYPE_F32 ? round_up(static_cast<size_t>(T) * K * 4, 256) : 0;
+  const size_t b_part = dtype == GMM_DTYPE_F32 ? round_up(static_cast<size_t>(E) * K * N * 4, 256) : 0;
+  return setup_and_launch(prm, A, B, static_cast<uint8_t*>(workspace), a_part, b_part, T, K, N, E, dtype,
+                          trans_b, tile_rows, prm.act, INT32_MAX, di, stream);
 }
 
 int gmm_sm100_device_error(int* status_out, int clear) {

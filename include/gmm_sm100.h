@@ -96,6 +96,58 @@ int gmm_sm100_forward_swiglu(const void* A, const void* B, const int64_t* batch_
                              int dtype, int trans_b, void* D, void* workspace,
                              size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------ device-resident MoE layer
+ * No reference counterpart (the reference's caller routes and permutes on its
+ * own; its benchmark leaves them out).  Every entry below only enqueues work
+ * on `stream` and never waits for the device, so a whole MoE layer can run
+ * without a host synchronisation. */
+
+/* Grouped GEMM whose batch sizes live in device memory: int32
+ * batch_sizes_dev[num_experts] (num_experts <= 1024).  A has rows_cap rows
+ * of which the first sum(batch_sizes) are used; D rows beyond the sum are not
+ * written.  If a size is negative or the sum exceeds rows_cap the kernel does
+ * no work and records GMM_ERR_INVALID_ARGUMENT / GMM_ERR_BATCH_SUM in the
+ * device error word.  swiglu != 0 selects the fused SwiGLU epilogue (see
+ * gmm_sm100_forward_swiglu).  Workspace: gmm_sm100_dev_workspace_size(). */
+int gmm_sm100_forward_dev(const void* A, const void* B, const int32_t* batch_sizes_dev,
+                          int64_t num_experts, int64_t rows_cap, int64_t dim, int64_t dim_out,
+                          int dtype, int trans_b, int swiglu, void* D, void* workspace,
+                          size_t workspace_bytes, void* stream);
+
+size_t gmm_sm100_dev_workspace_size(int64_t num_experts, int64_t rows_cap, int64_t dim,
+                                    int64_t dim_out, int dtype);
+
+/* Top-k routing: per token, softmax over the num_experts logits (fp32, bf16
+ * or fp16, row-major [num_tokens, num_experts]) and the k largest (ties to
+ * the lower expert index; k <= 8).  ids[t*k + j] (int32) in descending order;
+ * weights[t*k + j] (fp32) their probabilities, renormalised to sum 1 when
+ * renormalize != 0. */
+int gmm_sm100_moe_topk(const void* logits, int logits_dtype, int64_t num_tokens, int num_experts,
+                       int k, int renormalize, int32_t* ids, float* weights, void* stream);
+
+/* Permutation into expert order: a stable counting sort of the
+ * num_tokens * k (token, slot) pairs by ids[t*k + j].  Writes batch_sizes
+ * (int32[num_experts], rows per expert), dst_pos[t*k + j] (row of the pair
+ * in the permuted matrix; -1 for an id outside [0, num_experts)),
+ * src_token[row] (token of each permuted row) and, when x is non-null,
+ * x_perm[row] = x[src_token[row]] (rows of row_bytes bytes, a multiple of 16). */
+int gmm_sm100_moe_permute(const void* x, int64_t num_tokens, int64_t row_bytes, const int32_t* ids,
+                          int k, int num_experts, void* x_perm, int32_t* batch_sizes,
+                          int32_t* dst_pos, int32_t* src_token, void* workspace,
+                          size_t workspace_bytes, void* stream);
+
+size_t gmm_sm100_moe_permute_workspace_size(int64_t num_pairs, int num_experts);
+
+/* Combine: out[t] = sum_j weights[t*k + j] * y[dst_pos[t*k + j]] with fp32
+ * accumulation (weights may be NULL: plain sum); y is [num_tokens*k, dim_out]
+ * in expert order, dim_out a multiple of 8. */
+int gmm_sm100_moe_unpermute(const void* y, const int32_t* dst_pos, const float* weights,
+                            int64_t num_tokens, int k, int64_t dim_out, int dtype, void* out,
+                            void* stream);
+
+/* Detail of the last failure of a gmm_sm100_moe_* call on this thread. */
+const char* gmm_sm100_moe_last_error(void);
+
 /* Reads (and with clear != 0, resets) the device-side error word of the
  * current device: 0, or a gmm_status recorded by a kernel whose bounded wait
  * ran out.  Synchronises the device.  No reference counterpart (the

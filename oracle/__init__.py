@@ -122,6 +122,38 @@ def swiglu_oracle(a, b, batch_sizes, trans_b: bool = False) -> np.ndarray:
     return g / (1.0 + np.exp(-g)) * u
 
 
+def topk_oracle(logits, k: int, renormalize: bool = True):
+    """(ids [T, k], weights [T, k]) of softmax top-k routing, ties to the lower index."""
+    x = to_f32(logits).astype(np.float64)
+    order = np.argsort(-x, axis=1, kind="stable")[:, :k]
+    p = np.exp(x - x.max(axis=1, keepdims=True))
+    p /= p.sum(axis=1, keepdims=True)
+    w = np.take_along_axis(p, order, axis=1)
+    if renormalize:
+        w = w / w.sum(axis=1, keepdims=True)
+    return order.astype(np.int32), w
+
+
+def permute_oracle(ids, num_experts: int):
+    """Stable expert order of the (token, slot) pairs: (batch_sizes, dst_pos [T, k], src_token)."""
+    ids = np.asarray(ids)
+    T, k = ids.shape
+    flat = ids.reshape(-1)
+    order = np.argsort(flat, kind="stable")
+    dst = np.empty(T * k, dtype=np.int32)
+    dst[order] = np.arange(T * k, dtype=np.int32)
+    return (np.bincount(flat, minlength=num_experts).astype(np.int32), dst.reshape(T, k),
+            (order // k).astype(np.int32))
+
+
+def unpermute_oracle(y, dst_pos, weights=None) -> np.ndarray:
+    """out[t] = sum_j w[t, j] * y[dst_pos[t, j]] in float64."""
+    y64 = to_f32(y).astype(np.float64)
+    dst = np.asarray(dst_pos)
+    w = np.ones(dst.shape) if weights is None else to_f32(weights).astype(np.float64)
+    return np.einsum("tk,tkn->tn", w, y64[dst])
+
+
 def ref_gmm_port(a, b, batch_sizes, trans_b: bool = False):
     """The reference's ``ref_gmm`` (tests/test_forward.py:8-15) on torch CPU tensors.
 

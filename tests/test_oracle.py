@@ -85,3 +85,25 @@ def test_config_batch_sizes_are_frozen():
         assert int(bs.sum()) == cfg.rows
     assert min(frozen["3"]) == 0 and sum(v > 0 for v in frozen["3"]) == 240
     assert max(frozen["4"]) <= 16
+
+
+def test_routing_and_permutation_oracles_agree_with_loops():
+    rng = np.random.default_rng(0)
+    logits = rng.standard_normal((50, 12)).astype(np.float32)
+    logits[3, 5] = logits[3, 7] = 9.0  # a tie: the lower index wins
+    ids, w = oracle.topk_oracle(logits, 3, renormalize=True)
+    assert ids[3, 0] == 5 and ids[3, 1] == 7
+    for t in range(50):
+        want = sorted(range(12), key=lambda e: (-logits[t, e], e))[:3]
+        assert list(ids[t]) == want
+    np.testing.assert_allclose(w.sum(1), 1.0, rtol=1e-12)
+    bs, dst, src = oracle.permute_oracle(ids, 12)
+    rows = [(e, t, j) for t in range(50) for j in range(3) for e in [ids[t, j]]]
+    rows.sort(key=lambda r: r[0])  # stable: (token, slot) order kept within an expert
+    for pos, (e, t, j) in enumerate(rows):
+        assert dst[t, j] == pos and src[pos] == t
+    assert bs.sum() == 150 and list(bs) == [sum(1 for r in rows if r[0] == e) for e in range(12)]
+    y = rng.standard_normal((150, 4)).astype(np.float32)
+    out = oracle.unpermute_oracle(y, dst, w)
+    np.testing.assert_allclose(out[7], sum(w[7, j] * y[dst[7, j]].astype(np.float64) for j in range(3)),
+                               rtol=1e-6)
