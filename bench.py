@@ -55,6 +55,9 @@ def parse():
     ap.add_argument("--ffn", action="store_true",
                     help="time the MoE expert FFN (fused SwiGLU gate/up GEMM + down GEMM) on the "
                          "config's routing instead of the single grouped GEMM")
+    ap.add_argument("--layer", action="store_true",
+                    help="time the device-resident MoE layer (routing, permute, SwiGLU FFN, combine) "
+                         "eagerly and as a replayed CUDA graph")
     ap.add_argument("--kernel-only", action="store_true",
                     help="warm-up + timed launches only (no e2e / CPU baseline / clocks): the "
                          "command profiled with ncu")
@@ -436,8 +439,77 @@ def run_ffn(args):
         "gpu_launches": 2 * steps}), flush=True)
 
 
+def run_layer(args):
+    """Device-resident MoE layer on the config's shapes, eager and CUDA graph."""
+    import torch
+    from gmm_b200.configs import CONFIGS
+    from gmm_b200.moe import moe_forward
+    cid = args.config or 2
+    cfg = CONFIGS[cid]
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    E, dim, k, T = cfg.num_experts, cfg.dim, cfg.top_k, cfg.tokens
+    inter = cfg.dim_out // 2 if cid == 3 else cfg.dim_out
+    tb = cfg.trans_b
+    g = torch.Generator(device=dev).manual_seed(cfg.seed)
+    x = torch.randn(T, dim, generator=g, device=dev).to(cfg.dtype)
+    logits = torch.randn(T, E, generator=g, device=dev)
+    w1 = torch.empty(*((E, 2 * inter, dim) if tb else (E, dim, 2 * inter)), dtype=cfg.dtype, device=dev)
+    w2 = torch.empty(*((E, dim, inter) if tb else (E, inter, dim)), dtype=cfg.dtype, device=dev)
+    for e in range(E):
+        w1[e].copy_(torch.randn(w1.shape[1:], generator=g, device=dev) / math.sqrt(dim))
+        w2[e].copy_(torch.randn(w2.shape[1:], generator=g, device=dev) / math.sqrt(inter))
+    flops = 2.0 * T * k * dim * 2 * inter + 2.0 * T * k * inter * dim
+
+    def step():
+        return moe_forward(x, logits, w1, w2, k, tb, tb)
+
+    steps = max(1, min(args.steps, 50))
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    eager_ms = e0.elapsed_time(e1) / steps
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        step()
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(steps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    graph_ms = e0.elapsed_time(e1) / steps
+    del graph
+    print(json.dumps({
+        "metric": "device-resident MoE layer forward (route + permute + SwiGLU FFN + combine)",
+        "value": round(flops / (graph_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s", "n_gpus": 1,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": round(graph_ms, 4),
+        "eager_ms_per_step": round(eager_ms, 4), "tokens_per_s": round(T / (graph_ms * 1e-3), 1),
+        "higher_is_better": True, "dtype": {torch.bfloat16: "bf16", torch.float16: "fp16"}[cfg.dtype],
+        "data": "synthetic (router logits ~ N(0,1))",
+        "config": {"workload": f"cfg{cid} shapes, MoE layer", "tokens": T, "top_k": k, "experts": E,
+                   "dim": dim, "inter": inter, "trans_b": tb},
+        "gpu_launches": 7 * steps}), flush=True)
+
+
 def main():
     args = parse()
+    if args.layer and args.impl == "ours":
+        run_layer(args)
+        return
     if args.ffn and args.impl == "ours":
         run_ffn(args)
         return
