@@ -116,6 +116,30 @@ def moe_ffn(a: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.Tensor,
     return hopper_gmm_fwd(h, w_down, batch_sizes, trans_down)
 
 
+def gmm_vark(a: torch.Tensor, b: torch.Tensor, batch_sizes: torch.Tensor) -> torch.Tensor:
+    """Variable-K grouped GEMM (MoE backward weight gradient).
+
+    For each expert ``e`` with rows ``rows_e`` (from the CPU int64
+    ``batch_sizes``): ``out[e] = a[rows_e].T @ b[rows_e]``; ``a`` is
+    ``[T, M]``, ``b`` is ``[T, N]`` (bf16/fp16, CUDA), ``out`` is ``[E, M, N]``
+    with fp32 accumulation; an expert with no rows gets zeros.  The sibling of
+    the forward kernel that the reference removed from its extract.
+    """
+    from gmm_b200 import capi
+    import numpy as np
+    if a.dim() != 2 or b.dim() != 2 or a.shape[0] != b.shape[0]:
+        raise RuntimeError("a and b must be 2D with the same number of rows")
+    if not (a.is_cuda and b.is_cuda) or a.dtype != b.dtype:
+        raise RuntimeError("a and b must be CUDA tensors of one dtype")
+    a, b = a.contiguous(), b.contiguous()
+    bs = np.ascontiguousarray(batch_sizes.cpu().numpy().astype(np.int64))
+    out = torch.empty(bs.shape[0], a.shape[1], b.shape[1], dtype=a.dtype, device=a.device)
+    capi._check(capi.load().gmm_sm100_forward_vark(
+        a.data_ptr(), b.data_ptr(), bs.ctypes.data, bs.shape[0], a.shape[0], a.shape[1], b.shape[1],
+        capi.dtype_code(a.dtype), out.data_ptr(), torch.cuda.current_stream(a.device).cuda_stream))
+    return out
+
+
 def hopper_gmm_fwd_host(a, b, batch_sizes, trans_b=False, out=None, device=None):
     """``hopper_gmm_fwd`` on host-resident (pinned) operands, with the transfers pipelined
     against the GEMM; see :mod:`gmm_b200.streaming`."""

@@ -76,7 +76,9 @@ struct __align__(64) GmmParams {
   int dev_experts;
   int rows_cap;
   int tile_rows;  // 128 or 256 (m-tile height the device table is built for)
-  int pad2_;
+  int vk_m;        // variable-K kernel: rows of each D[e] (= columns of A)
+  int vk_m_tiles;  // variable-K kernel: 128-row tiles per D[e]
+  int pad3_;
   void* d_peer[kMaxPeers];  // each rank's output buffer (remote mode)
   // Table of the non-empty groups, laid out as
   //   row_off[G+1] | tile_off[G+1] | expert[G] [| src_off[G][W+1] | dst_row[G][W]]
@@ -290,29 +292,35 @@ __device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
 // XOR-swizzled by row, conflict-free both ways) so that every store
 // instruction writes four whole 128-byte row segments (8 lanes per row): full
 // L2 lines locally, and large NVLink writes when the row lives on a peer.
+// Drains one 32-row slab of an accumulator -- TMEM lanes [32q, 32q + 32) of
+// columns [taddr, taddr + BN) -- into the rows rp[] (8 per lane: rows
+// i*4 + lane/8; null = not stored).  Each thread converts its own row; the rows
+// then pass through `stage` (32 rows x 128 B, 16-byte chunks XOR-swizzled by
+// row, conflict-free both ways) so that every store instruction writes four
+// whole 128-byte row segments (8 lanes per row): full L2 lines locally, and
+// large NVLink writes when the row lives on a peer.  zero = store zeros
+// without reading TMEM (a tile whose contraction is empty).
 template <typename OutT, int BN>
-__device__ __forceinline__ void drain_slab(const GmmParams& p, const TableView& tv, int g,
-                                           int slab_row0, int slab_rows, int n0, uint32_t taddr,
-                                           uint32_t stage, int lane) {
+__device__ __forceinline__ void drain_rows(OutT* const (&rp)[8], int n0, int dim_out, uint32_t taddr,
+                                           uint32_t stage, int lane, bool zero = false) {
   constexpr int kColsPerSeg = 128 / static_cast<int>(sizeof(OutT));  // 64 (16-bit) or 32 (fp32)
   constexpr int kElemsPer16 = 16 / static_cast<int>(sizeof(OutT));
-  OutT* rp[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int rr = i * 4 + (lane >> 3);
-    rp[i] = rr < slab_rows ? out_row<OutT>(p, tv, g, slab_row0 + rr) : nullptr;
-  }
   const int ch = lane & 7;
   const uint32_t my_row = stage + lane * 128;
 #pragma unroll 1
   for (int c0 = 0; c0 < BN; c0 += kColsPerSeg) {
     const int col = n0 + c0;
-    if (col >= p.dim_out) break;  // warp-uniform
+    if (col >= dim_out) break;  // warp-uniform
 #pragma unroll
     for (int h = 0; h < kColsPerSeg / 32; ++h) {
       uint32_t v[32];
-      tmem_ld_32x32b_x32(taddr + c0 + h * 32, v);
-      tmem_wait_ld();
+      if (!zero) {
+        tmem_ld_32x32b_x32(taddr + c0 + h * 32, v);
+        tmem_wait_ld();
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = 0u;
+      }
       if constexpr (sizeof(OutT) == 2) {
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -335,11 +343,25 @@ __device__ __forceinline__ void drain_slab(const GmmParams& p, const TableView& 
     for (int i = 0; i < 8; ++i) {
       const int rr = i * 4 + (lane >> 3);
       const uint4 val = ld_shared_v4(stage + rr * 128 + ((ch ^ (rr & 7)) << 4));
-      if (rp[i] && col + ch * kElemsPer16 < p.dim_out)
+      if (rp[i] && col + ch * kElemsPer16 < dim_out)
         *reinterpret_cast<uint4*>(rp[i] + col + ch * kElemsPer16) = val;
     }
     __syncwarp();
   }
+}
+
+// drain_rows for a slab of grouped-GEMM rows: destinations from out_row().
+template <typename OutT, int BN>
+__device__ __forceinline__ void drain_slab(const GmmParams& p, const TableView& tv, int g,
+                                           int slab_row0, int slab_rows, int n0, uint32_t taddr,
+                                           uint32_t stage, int lane) {
+  OutT* rp[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int rr = i * 4 + (lane >> 3);
+    rp[i] = rr < slab_rows ? out_row<OutT>(p, tv, g, slab_row0 + rr) : nullptr;
+  }
+  drain_rows<OutT, BN>(rp, n0, p.dim_out, taddr, stage, lane);
 }
 
 __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + __expf(-g)) * u; }
@@ -705,6 +727,7 @@ __global__ void __launch_bounds__(256) ep_gather_kernel(const __grid_constant__ 
 }
 
 #include "gmm_pair_kernel.cuh"
+#include "gmm_vark_kernel.cuh"
 
 }  // namespace gmm_sm100
 
@@ -1313,6 +1336,85 @@ int gmm_sm100_forward_dev(const void* A, const void* B, const int32_t* batch_siz
   const size_t b_part = dtype == GMM_DTYPE_F32 ? round_up(static_cast<size_t>(E) * K * N * 4, 256) : 0;
   return setup_and_launch(prm, A, B, static_cast<uint8_t*>(workspace), a_part, b_part, T, K, N, E, dtype,
                           trans_b, tile_rows, prm.act, INT32_MAX, di, stream);
+}
+
+int gmm_sm100_forward_vark(const void* A, const void* B, const int64_t* batch_sizes, int64_t num_experts,
+                           int64_t num_tokens, int64_t dim_a, int64_t dim_b, int dtype, void* D,
+                           void* stream_ptr) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  const int64_t E = num_experts, T = num_tokens, M = dim_a, N = dim_b;
+  if (E < 0 || T < 0 || M < 0 || N < 0) return fail(GMM_ERR_INVALID_ARGUMENT, "negative size");
+  if (E > 0 && !batch_sizes) return fail(GMM_ERR_INVALID_ARGUMENT, "batch_sizes is null");
+  if (dtype != GMM_DTYPE_BF16 && dtype != GMM_DTYPE_F16)
+    return fail(GMM_ERR_DTYPE, "the variable-K grouped GEMM takes bf16 / fp16");
+  if (E + 1 > kInlineTableInts) return fail(GMM_ERR_TOO_LARGE, "too many experts for the variable-K kernel");
+  int64_t sum = 0;
+  for (int64_t e = 0; e < E; ++e) {
+    if (batch_sizes[e] < 0) return fail(GMM_ERR_INVALID_ARGUMENT, "batch_sizes[" + std::to_string(e) + "] is negative");
+    sum += batch_sizes[e];
+  }
+  if (sum != T)
+    return fail(GMM_ERR_BATCH_SUM, "Sum of batch_sizes (" + std::to_string(sum) + ") must equal A.size(0) (" +
+                                       std::to_string(T) + ")");
+  if (E == 0 || M == 0 || N == 0) return GMM_OK;
+  if (T > INT32_MAX - 256 || M > INT32_MAX || N > INT32_MAX) return fail(GMM_ERR_TOO_LARGE, "too large");
+  if ((M * 2) % 16 != 0 || (N * 2) % 16 != 0)
+    return fail(GMM_ERR_ALIGNMENT, "A and B row pitches must be multiples of 16 bytes");
+  if (!D || !aligned16(D)) return fail(GMM_ERR_ALIGNMENT, "D must be non-null and 16-byte aligned");
+  int dev = 0;
+  cudaError_t ce = cudaGetDevice(&dev);
+  if (ce != cudaSuccess) return cuda_fail(ce, "cudaGetDevice");
+  DeviceInfo* di = nullptr;
+  int rc = device_info(dev, &di);
+  if (rc != GMM_OK) return rc;
+  if (T == 0) {  // every expert is empty: D = 0
+    ce = cudaMemsetAsync(D, 0, static_cast<size_t>(E) * M * N * 2, stream);
+    return ce == cudaSuccess ? GMM_OK : cuda_fail(ce, "cudaMemsetAsync");
+  }
+  if (!A || !B || !aligned16(A) || !aligned16(B))
+    return fail(GMM_ERR_ALIGNMENT, "A and B must be non-null and 16-byte aligned");
+  const int64_t m_tiles = (M + 127) / 128, n_tiles = (N + 255) / 256;
+  const int64_t total = E * m_tiles * n_tiles;
+  if (total > INT32_MAX) return fail(GMM_ERR_TOO_LARGE, "too many output tiles");
+  GmmParams prm;
+  std::memset(&prm, 0, sizeof(prm));
+  prm.d = D;
+  prm.ldd = N;
+  prm.dim_out = static_cast<int>(N);
+  prm.n_tiles = static_cast<int>(n_tiles);
+  prm.vk_m = static_cast<int>(M);
+  prm.vk_m_tiles = static_cast<int>(m_tiles);
+  prm.total_tiles = static_cast<int>(total);
+  prm.num_groups = static_cast<int>(E);
+  int64_t row = 0;
+  for (int64_t e = 0; e < E; ++e) {
+    prm.inline_table[e] = static_cast<int32_t>(row);
+    row += batch_sizes[e];
+  }
+  prm.inline_table[E] = static_cast<int32_t>(row);
+  const CUtensorMapDataType tt =
+      dtype == GMM_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const cuuint64_t adims[2] = {static_cast<cuuint64_t>(M), static_cast<cuuint64_t>(T)};
+  const cuuint64_t astr[1] = {static_cast<cuuint64_t>(M) * 2};
+  const cuuint64_t bdims[2] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(T)};
+  const cuuint64_t bstr[1] = {static_cast<cuuint64_t>(N) * 2};
+  const cuuint32_t box[2] = {64, 64};
+  if ((rc = encode(&prm.tmap_a, tt, 2, A, adims, astr, box)) || (rc = encode(&prm.tmap_b, tt, 2, B, bdims, bstr, box)))
+    return rc;
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(total, di->sm_count)));
+  const int bit = dtype == GMM_DTYPE_BF16 ? 9 : 10;
+  auto launch = [&](auto kern, int smem) -> int {
+    if (!(di->smem_attr_set.load() & (1u << bit))) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(vark)");
+      di->smem_attr_set.fetch_or(1u << bit);
+    }
+    kern<<<grid, kThreads, smem, stream>>>(prm);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? GMM_OK : cuda_fail(e, "variable-K kernel launch");
+  };
+  return dtype == GMM_DTYPE_BF16 ? launch(gmm_vark_kernel<kKindBf16>, VarKCfg<kKindBf16>::kSmemBytes)
+                                 : launch(gmm_vark_kernel<kKindF16>, VarKCfg<kKindF16>::kSmemBytes);
 }
 
 int gmm_sm100_device_error(int* status_out, int clear) {

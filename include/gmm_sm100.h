@@ -96,6 +96,18 @@ int gmm_sm100_forward_swiglu(const void* A, const void* B, const int64_t* batch_
                              int dtype, int trans_b, void* D, void* workspace,
                              size_t workspace_bytes, void* stream);
 
+/* Variable-K grouped GEMM (MoE backward weight gradient): for each expert e
+ * with rows [off_e, off_e + batch_sizes[e]) of A [num_tokens, dim_a] and
+ * B [num_tokens, dim_b] (both row-major),
+ *   D[e] = A[rows_e]^T @ B[rows_e]      D is [num_experts, dim_a, dim_b]
+ * accumulated in fp32; an expert with no rows gets D[e] = 0.  bf16 / fp16;
+ * num_experts <= 3073.  Restores the kernel family the reference removed
+ * from its forward-only extract (reference csrc/hopper_gmm_forward.cu:16-21,
+ * CutlassGroupedGemmVariableK). */
+int gmm_sm100_forward_vark(const void* A, const void* B, const int64_t* batch_sizes,
+                           int64_t num_experts, int64_t num_tokens, int64_t dim_a, int64_t dim_b,
+                           int dtype, void* D, void* stream);
+
 /* ------------------------------------------------ device-resident MoE layer
  * No reference counterpart (the reference's caller routes and permutes on its
  * own; its benchmark leaves them out).  Every entry below only enqueues work

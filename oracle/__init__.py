@@ -122,6 +122,19 @@ def swiglu_oracle(a, b, batch_sizes, trans_b: bool = False) -> np.ndarray:
     return g / (1.0 + np.exp(-g)) * u
 
 
+def vark_oracle(a, b, batch_sizes) -> np.ndarray:
+    """D[e] = a[rows_e]^T @ b[rows_e] in float64 ([E, M, N]); zeros for empty experts."""
+    a64, b64 = to_f32(a).astype(np.float64), to_f32(b).astype(np.float64)
+    bs = _bs_list(batch_sizes)
+    out = np.zeros((len(bs), a64.shape[1], b64.shape[1]))
+    start = 0
+    for e, m in enumerate(bs):
+        if m:
+            out[e] = a64[start:start + m].T @ b64[start:start + m]
+        start += m
+    return out
+
+
 def topk_oracle(logits, k: int, renormalize: bool = True):
     """(ids [T, k], weights [T, k]) of softmax top-k routing, ties to the lower index."""
     x = to_f32(logits).astype(np.float64)
