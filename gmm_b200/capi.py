@@ -59,10 +59,10 @@ _SIGNATURES = {
                                                ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]),
     "gmm_sm100_moe_last_error": (ctypes.c_char_p, []),
     "gmm_sm100_ep_gather": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
-                                           ctypes.c_void_p, ctypes.c_int64, ctypes.c_int,
+                                           ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_int,
                                            ctypes.c_int64, ctypes.c_void_p]),
     "gmm_sm100_forward_ep": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
-                                            ctypes.c_void_p, ctypes.c_int64, ctypes.c_int,
+                                            ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_int,
                                             ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
                                             ctypes.c_int64, ctypes.c_int, ctypes.c_int,
                                             ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
@@ -152,16 +152,17 @@ def _ptrs(values):
     return (ctypes.c_void_p * len(values))(*[int(v) for v in values])
 
 
-def ep_gather(x, src_ptrs, counts, src_rows, num_local_experts, row_bytes, stream=None):
-    """Pull the (expert, source) row chunks into ``x`` (see ``gmm_sm100_ep_gather``)."""
+def ep_gather(x, src_ptrs, counts, src_rows, num_local_experts, row_bytes, rank_base=0, stream=None):
+    """Pull the (expert, segment) row chunks into ``x`` (see ``gmm_sm100_ep_gather``)."""
     import torch
     c, r = _i64(counts), _i64(src_rows)
     s = torch.cuda.current_stream(x.device).cuda_stream if stream is None else stream
     _check(load().gmm_sm100_ep_gather(x.data_ptr(), _ptrs(src_ptrs), c.ctypes.data, r.ctypes.data,
-                                      num_local_experts, len(src_ptrs), row_bytes, s))
+                                      num_local_experts, len(src_ptrs), rank_base, row_bytes, s))
 
 
-def forward_ep(x, b, counts, dst_rows, num_local_experts, out_ptrs, trans_b=False, stream=None):
+def forward_ep(x, b, counts, dst_rows, num_local_experts, out_ptrs, trans_b=False, rank_base=0,
+               stream=None):
     """Local grouped GEMM whose epilogue writes each row back to its source rank."""
     import torch
     c, d = _i64(counts), _i64(dst_rows)
@@ -175,5 +176,5 @@ def forward_ep(x, b, counts, dst_rows, num_local_experts, out_ptrs, trans_b=Fals
     ws = torch.empty(need, dtype=torch.uint8, device=x.device) if need else None
     s = torch.cuda.current_stream(x.device).cuda_stream if stream is None else stream
     _check(lib.gmm_sm100_forward_ep(x.data_ptr(), b.data_ptr(), c.ctypes.data, d.ctypes.data,
-                                    num_local_experts, W, _ptrs(out_ptrs), x.shape[0], dim, dim_out,
+                                    num_local_experts, W, rank_base, _ptrs(out_ptrs), x.shape[0], dim, dim_out,
                                     dtype, int(bool(trans_b)), ws.data_ptr() if need else None, need, s))

@@ -78,7 +78,7 @@ struct __align__(64) GmmParams {
   int tile_rows;  // 128 or 256 (m-tile height the device table is built for)
   int vk_m;        // variable-K kernel: rows of each D[e] (= columns of A)
   int vk_m_tiles;  // variable-K kernel: 128-row tiles per D[e]
-  int pad3_;
+  int ep_rank_base;  // remote mode: segment j of a group comes from rank (ep_rank_base + j) % world
   void* d_peer[kMaxPeers];  // each rank's output buffer (remote mode)
   // Table of the non-empty groups, laid out as
   //   row_off[G+1] | tile_off[G+1] | expert[G] [| src_off[G][W+1] | dst_row[G][W]]
@@ -228,10 +228,12 @@ __device__ __forceinline__ T* out_row(const GmmParams& p, const TableView& tv, i
   if (!p.remote) return reinterpret_cast<T*>(p.d) + static_cast<long long>(row) * p.ldd;
   const int grow = row - tv.row_off[g];
   const int32_t* so = tv.src_off + g * (p.world + 1);
-  int s = 0;
-  while (s + 1 < p.world && grow >= so[s + 1]) ++s;
+  int j = 0;  // segment of the row inside its group
+  while (j + 1 < p.world && grow >= so[j + 1]) ++j;
   const int32_t* dr = tv.dst_row + g * p.world;
-  return reinterpret_cast<T*>(p.d_peer[s]) + static_cast<long long>(dr[s] + grow - so[s]) * p.ldd;
+  int s = p.ep_rank_base + j;
+  if (s >= p.world) s -= p.world;
+  return reinterpret_cast<T*>(p.d_peer[s]) + static_cast<long long>(dr[j] + grow - so[j]) * p.ldd;
 }
 
 struct Tile {
@@ -945,8 +947,9 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 struct EpRoute {
   int world;
   void* const* out_peers;
-  const int64_t* counts;
-  const int64_t* dst_rows;
+  const int64_t* counts;    // [E_local][world], segment order
+  const int64_t* dst_rows;  // [E_local][world], segment order
+  int rank_base;            // segment j comes from rank (rank_base + j) % world
 };
 
 // Append src_off[G][W+1] | dst_row[G][W] for the non-empty groups and decide
@@ -1120,6 +1123,7 @@ int forward_impl(const void* A, const void* B, const int64_t* batch_sizes, int64
   if (ep) {
     prm.remote = 1;
     prm.world = ep->world;
+    prm.ep_rank_base = ((ep->rank_base % ep->world) + ep->world) % ep->world;
     for (int s = 0; s < ep->world; ++s) prm.d_peer[s] = ep->out_peers[s];
   }
   uint8_t* ws = static_cast<uint8_t*>(workspace);
@@ -1188,13 +1192,13 @@ size_t gmm_sm100_ep_workspace_size(const int64_t* counts, int64_t num_local_expe
     for (int s = 0; s < world; ++s) local_bs[e] += counts[e * world + s];
   Plan pl;
   if (make_plan(local_bs.data(), num_local_experts, num_rows, dim, dim_out, dtype, pl) != GMM_OK) return 0;
-  EpRoute route{world, nullptr, counts, zeros.data()};
+  EpRoute route{world, nullptr, counts, zeros.data(), 0};
   if (!append_ep_table(pl, local_bs.data(), num_local_experts, route)) return 0;
   return pl.split_bytes + pl.table_bytes;
 }
 
 int gmm_sm100_forward_ep(const void* X, const void* B, const int64_t* counts, const int64_t* dst_rows,
-                         int64_t num_local_experts, int world, void* const* out_peers,
+                         int64_t num_local_experts, int world, int rank_base, void* const* out_peers,
                          int64_t num_rows, int64_t dim, int64_t dim_out, int dtype, int trans_b,
                          void* workspace, size_t workspace_bytes, void* stream) {
   if (!counts || !dst_rows || num_local_experts < 0 || world < 1 || world > kMaxPeers)
@@ -1205,13 +1209,13 @@ int gmm_sm100_forward_ep(const void* X, const void* B, const int64_t* counts, co
       if (counts[e * world + s] < 0) return fail(GMM_ERR_INVALID_ARGUMENT, "negative row count");
       local_bs[e] += counts[e * world + s];
     }
-  EpRoute route{world, out_peers, counts, dst_rows};
+  EpRoute route{world, out_peers, counts, dst_rows, rank_base};
   return forward_impl(X, B, local_bs.data(), num_local_experts, num_rows, dim, dim_out, dtype, trans_b,
                       nullptr, workspace, workspace_bytes, stream, &route);
 }
 
 int gmm_sm100_ep_gather(void* X, const void* const* src_peers, const int64_t* counts,
-                        const int64_t* src_rows, int64_t num_local_experts, int world,
+                        const int64_t* src_rows, int64_t num_local_experts, int world, int rank_base,
                         int64_t row_bytes, void* stream_ptr) {
   if (!counts || !src_rows || !src_peers || world < 1 || world > kMaxPeers || num_local_experts < 0)
     return fail(GMM_ERR_INVALID_ARGUMENT, "bad gather arguments");
@@ -1222,15 +1226,16 @@ int gmm_sm100_ep_gather(void* X, const void* const* src_peers, const int64_t* co
   std::memset(&prm, 0, sizeof(prm));
   int64_t rows = 0;
   int n = 0;
+  const int base = ((rank_base % world) + world) % world;
   for (int64_t e = 0; e < num_local_experts; ++e)
-    for (int s = 0; s < world; ++s) {
-      const int64_t m = counts[e * world + s];
-      if (m < 0 || src_rows[e * world + s] < 0) return fail(GMM_ERR_INVALID_ARGUMENT, "negative count or row");
+    for (int j = 0; j < world; ++j) {
+      const int64_t m = counts[e * world + j];
+      if (m < 0 || src_rows[e * world + j] < 0) return fail(GMM_ERR_INVALID_ARGUMENT, "negative count or row");
       if (m == 0) continue;
       if (n >= kMaxGatherChunks) return fail(GMM_ERR_TOO_LARGE, "too many (expert, rank) chunks");
       prm.chunk_dst[n] = static_cast<int>(rows);
-      prm.chunk_rank[n] = s;
-      prm.chunk_row[n] = static_cast<int>(src_rows[e * world + s]);
+      prm.chunk_rank[n] = (base + j) % world;
+      prm.chunk_row[n] = static_cast<int>(src_rows[e * world + j]);
       ++n;
       rows += m;
     }

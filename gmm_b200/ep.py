@@ -231,14 +231,18 @@ class ExpertParallelGmm:
         # offsets of every global expert's rows in every rank's layout: [W, E]
         offs = torch.cumsum(all_bs, dim=1) - all_bs
         mine = slice(r * El, (r + 1) * El)
-        counts = all_bs[:, mine].t().contiguous().numpy()   # [El, W]: rows of local e from s
-        rows_at = offs[:, mine].t().contiguous().numpy()    # where they sit on s
+        # segment j of every local expert comes from rank (r + j) % W: each rank
+        # starts with itself and walks the others in a rotated order, so no two
+        # ranks read from or write to the same peer at the same time
+        order = [(r + j) % W for j in range(W)]
+        counts = all_bs[order][:, mine].t().contiguous().numpy()  # [El, W]
+        rows_at = offs[order][:, mine].t().contiguous().numpy()   # where they sit on their rank
         n_recv = int(counts.sum())
         x = self._buffer("_x", n_recv, dim, a)
         self._barrier(a.device)  # every rank's token rows are in place
         if n_recv:
-            capi.ep_gather(x, sym[7], counts, rows_at, El, dim * a.element_size())
-            capi.forward_ep(x, b_local, counts, rows_at, El, sym[8], trans_b=trans_b)
+            capi.ep_gather(x, sym[7], counts, rows_at, El, dim * a.element_size(), rank_base=r)
+            capi.forward_ep(x, b_local, counts, rows_at, El, sym[8], trans_b=trans_b, rank_base=r)
         self._barrier(a.device)  # every peer's result rows have landed here
         return out
 

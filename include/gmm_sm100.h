@@ -168,26 +168,29 @@ int gmm_sm100_device_error(int* status_out, int clear);
 
 /* ---------------------------------------------------------------- expert parallelism
  * No reference counterpart (the reference runs on one GPU).  A rank owning
- * num_local_experts experts receives, for local expert e, counts[e*world + s]
- * rows from each source rank s, stored expert-major in X (all sources of
- * expert 0, then of expert 1, ...).  The pointers in out_peers / src_peers are
- * device addresses valid on the calling device (peer memory of the other
- * ranks, e.g. symmetric-memory buffers); world <= 8. */
+ * num_local_experts experts receives, for local expert e, world segments of
+ * rows stored expert-major in X: segment j (j = 0..world-1) comes from rank
+ * s = (rank_base + j) % world and holds counts[e*world + j] rows.  Passing
+ * its own rank as rank_base makes every rank start with a different peer, so
+ * at any moment the ranks read from / write to distinct peers.  The pointers
+ * in out_peers / src_peers (indexed by rank) are device addresses valid on
+ * the calling device (peer memory of the other ranks, e.g. symmetric-memory
+ * buffers); world <= 8. */
 
-/* Dispatch: copy every (expert, source) chunk of rows into X, reading
- * src_peers[s] + src_rows[e*world + s] * row_bytes over NVLink. */
+/* Dispatch: copy every (expert, segment) chunk of rows into X, reading
+ * src_peers[s] + src_rows[e*world + j] * row_bytes over NVLink. */
 int gmm_sm100_ep_gather(void* X, const void* const* src_peers, const int64_t* counts,
                         const int64_t* src_rows, int64_t num_local_experts, int world,
-                        int64_t row_bytes, void* stream);
+                        int rank_base, int64_t row_bytes, void* stream);
 
 /* Local grouped GEMM with the combine fused into its epilogue: the result of
- * each row of X goes straight to row dst_rows[e*world + s] + i of
- * out_peers[s] (the rank the row came from).  B holds the local experts'
- * weights ([E_local, dim, dim_out], or [E_local, dim_out, dim] if trans_b).
- * The caller orders the peers' reads/writes with a cross-rank barrier
- * before and after. */
+ * row i of segment j of local expert e goes straight to row
+ * dst_rows[e*world + j] + i of out_peers[s] (s = the rank the row came
+ * from).  B holds the local experts' weights ([E_local, dim, dim_out], or
+ * [E_local, dim_out, dim] if trans_b).  The caller orders the peers'
+ * reads/writes with a cross-rank barrier before and after. */
 int gmm_sm100_forward_ep(const void* X, const void* B, const int64_t* counts, const int64_t* dst_rows,
-                         int64_t num_local_experts, int world, void* const* out_peers,
+                         int64_t num_local_experts, int world, int rank_base, void* const* out_peers,
                          int64_t num_rows, int64_t dim, int64_t dim_out, int dtype, int trans_b,
                          void* workspace, size_t workspace_bytes, void* stream);
 
