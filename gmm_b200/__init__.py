@@ -38,11 +38,19 @@ def _load_c_ext() -> bool:
     return True
 
 
-if _load_c_ext():
+def load_native() -> bool:
+    """Load ``_C.so`` (registering the ops and their fake impls) if not done yet.
+
+    Called at import; a build run in the same process calls it again once the
+    library exists."""
+    global _HAS_C
+    if _HAS_C:
+        return True
+    if not _load_c_ext():
+        return False
     _HAS_C = True
-else:
-    warnings.warn("gmm_b200._C not built; run `python -m gmm_b200.build`. "
-                  f"No _C.so found in {_PKG_DIR}", RuntimeWarning)
+    _register_fakes()
+    return True
 
 
 def hopper_gmm_fwd(a: torch.Tensor,
@@ -68,24 +76,6 @@ def hopper_gmm_fwd(a: torch.Tensor,
     if not _HAS_C:
         raise RuntimeError("gmm_b200._C is not available. Build with `python -m gmm_b200.build`.")
     return torch.ops.hopper_gmm_fwd.gmm(a, b, batch_sizes, trans_b)
-
-
-if _HAS_C:
-    @torch.library.register_fake("hopper_gmm_fwd::gmm")
-    def _hopper_gmm_fwd_fake(a, b, batch_sizes, trans_b):
-        num_tokens = a.shape[0]
-        n = b.shape[1] if trans_b else b.shape[2]
-        return torch.empty(num_tokens, n, dtype=a.dtype, device=a.device)
-
-    def _gmm_swiglu_fake(a, b, batch_sizes, trans_b):
-        n = b.shape[1] if trans_b else b.shape[2]
-        return torch.empty(a.shape[0], n // 2, dtype=a.dtype, device=a.device)
-
-    try:  # absent only in a stale build; `python -m gmm_b200.build` refreshes it
-        torch.library.register_fake("hopper_gmm_fwd::gmm_swiglu")(_gmm_swiglu_fake)
-    except RuntimeError:
-        warnings.warn("gmm_b200._C predates gmm_swiglu; rebuild with `python -m gmm_b200.build`",
-                      RuntimeWarning)
 
 
 def gmm_swiglu(a: torch.Tensor, b: torch.Tensor, batch_sizes: torch.Tensor,
@@ -147,6 +137,29 @@ def hopper_gmm_fwd_host(a, b, batch_sizes, trans_b=False, out=None, device=None)
         raise RuntimeError("gmm_b200._C is not available. Build with `python -m gmm_b200.build`.")
     from gmm_b200.streaming import hopper_gmm_fwd_host as _f
     return _f(a, b, batch_sizes, trans_b=trans_b, out=out, device=device)
+
+
+def _register_fakes() -> None:
+    @torch.library.register_fake("hopper_gmm_fwd::gmm")
+    def _hopper_gmm_fwd_fake(a, b, batch_sizes, trans_b):
+        num_tokens = a.shape[0]
+        n = b.shape[1] if trans_b else b.shape[2]
+        return torch.empty(num_tokens, n, dtype=a.dtype, device=a.device)
+
+    def _gmm_swiglu_fake(a, b, batch_sizes, trans_b):
+        n = b.shape[1] if trans_b else b.shape[2]
+        return torch.empty(a.shape[0], n // 2, dtype=a.dtype, device=a.device)
+
+    try:  # absent only in a stale build; `python -m gmm_b200.build` refreshes it
+        torch.library.register_fake("hopper_gmm_fwd::gmm_swiglu")(_gmm_swiglu_fake)
+    except RuntimeError:
+        warnings.warn("gmm_b200._C predates gmm_swiglu; rebuild with `python -m gmm_b200.build`",
+                      RuntimeWarning)
+
+
+if not load_native():
+    warnings.warn("gmm_b200._C not built; run `python -m gmm_b200.build`. "
+                  f"No loadable _C.so in {_PKG_DIR}", RuntimeWarning)
 
 
 __all__ = ["hopper_gmm_fwd"]
