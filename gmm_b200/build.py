@@ -28,6 +28,7 @@ TORCH_OP = os.path.join(PKG, "_C.so")
 KERNEL_SOURCES = [os.path.join(CSRC, f) for f in ("gmm_sm100.cu", "moe_sm100.cu")]
 KERNEL_HEADERS = [os.path.join(CSRC, "sm100_ptx.cuh"), os.path.join(CSRC, "gmm_pair_kernel.cuh"),
                   os.path.join(CSRC, "gmm_vark_kernel.cuh"),
+                  os.path.join(CSRC, "gmm_swap_kernel.cuh"),
                   os.path.join(INCLUDE, "gmm_sm100.h")]
 
 

@@ -15,6 +15,10 @@
 //     output type and store rows that belong to the tile's expert -- rows past
 //     an expert's segment are never written, which keeps output placement exact.
 //
+// bf16/fp16 problems whose experts are small or ragged go to the swap-AB
+// kernel of gmm_swap_kernel.cuh instead (output columns on the MMA's M,
+// token rows on its N, row blocks sized to the expert).
+//
 // A is addressed through one 2D tensor map over all T rows (a tile of expert
 // g starts at row off_g + 128 m); B through one 3D tensor map whose outer
 // coordinate is the expert.  No per-expert descriptors, no TMA multicast.
@@ -730,6 +734,7 @@ __global__ void __launch_bounds__(256) ep_gather_kernel(const __grid_constant__ 
 
 #include "gmm_pair_kernel.cuh"
 #include "gmm_vark_kernel.cuh"
+#include "gmm_swap_kernel.cuh"
 
 }  // namespace gmm_sm100
 
@@ -768,7 +773,10 @@ struct DeviceInfo {
   std::atomic<int> state{0};  // 0 unknown, 1 ok, 2 wrong arch
   int sm_count = 0;
   int cc_major = 0, cc_minor = 0;
-  std::atomic<unsigned> smem_attr_set{0};  // bit per kernel variant
+  // Bit per kernel variant whose shared-memory attribute is set: 0 fp32;
+  // 1-4 128-row bf16/fp16 x NT/NN; 5-8 CTA pair; 9-10 variable-K bf16/fp16;
+  // 11-14 swap-AB bf16/fp16 x NT/NN.
+  std::atomic<unsigned> smem_attr_set{0};
   int pair_clusters[16] = {};               // resident CTA pairs per pair-kernel variant
 };
 DeviceInfo g_dev[kMaxDevices];
@@ -925,17 +933,44 @@ int launch_pair(const GmmParams& prm, int total_tiles, cudaStream_t stream, Devi
   return GMM_OK;
 }
 
-// Tile rows for a 16-bit problem: 256-row CTA-pair tiles when the non-empty
-// experts average at least 384 rows, else 128-row single-CTA tiles.
-// GMM_SM100_TILE=128 or =256 forces one of them (tests and benchmarks).
-int64_t choose_tile_rows(const int64_t* bs, int64_t E, int64_t T, int dtype) {
-  if (dtype == GMM_DTYPE_F32) return 128;
+template <int kKind, bool kMn>
+int launch_swap(const GmmParams& prm, int grid, cudaStream_t stream, DeviceInfo* di, int bit) {
+  using C = SwapCfg<kKind, kMn>;
+  auto kern = gmm_swap_kernel<kKind, kMn>;
+  if (!(di->smem_attr_set.load() & (1u << bit))) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(swap)");
+    di->smem_attr_set.fetch_or(1u << bit);
+  }
+  kern<<<grid, kThreads, C::kSmemBytes, stream>>>(prm);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "gmm swap kernel launch");
+  return GMM_OK;
+}
+
+// Tile kind of a problem.  fp32: 128-row tiles.  16-bit: CTA-pair 256-row
+// tiles when the non-empty experts average at least 384 rows; swap-AB tiles
+// when no expert has more than 64 rows (decode-shaped routing, where a
+// 128-row tile would be at least half padding) and neither the SwiGLU nor the
+// expert-parallel epilogue is needed; else single-CTA 128-row tiles.
+// GMM_SM100_TILE=128 / 256 / swap forces one of them (swap falls back to 128
+// for the SwiGLU and expert-parallel epilogues, which it does not have).
+enum TileKind { kTile128 = 0, kTilePair = 1, kTileSwap = 2 };
+
+TileKind choose_tile_kind(const int64_t* bs, int64_t E, int64_t T, int dtype, int act, bool remote) {
+  if (dtype == GMM_DTYPE_F32) return kTile128;
+  const bool swap_ok = !act && !remote;
   const char* force = std::getenv("GMM_SM100_TILE");
-  if (force && std::strcmp(force, "128") == 0) return 128;
-  if (force && std::strcmp(force, "256") == 0) return 256;
-  int64_t groups = 0;
-  for (int64_t e = 0; e < E; ++e) groups += bs[e] > 0;
-  return (groups > 0 && T >= 384 * groups) ? 256 : 128;
+  if (force && std::strcmp(force, "128") == 0) return kTile128;
+  if (force && std::strcmp(force, "256") == 0) return kTilePair;
+  if (force && std::strcmp(force, "swap") == 0) return swap_ok ? kTileSwap : kTile128;
+  int64_t groups = 0, max_m = 0;
+  for (int64_t e = 0; e < E; ++e) {
+    groups += bs[e] > 0;
+    max_m = std::max(max_m, bs[e]);
+  }
+  if (groups > 0 && T >= 384 * groups) return kTilePair;
+  return (swap_ok && max_m <= 64) ? kTileSwap : kTile128;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -981,7 +1016,8 @@ bool append_ep_table(Plan& pl, const int64_t* local_bs, int64_t E, const EpRoute
 // count when the host knows it).
 int setup_and_launch(GmmParams& prm, const void* A, const void* B, uint8_t* ws, size_t a_part,
                      size_t b_part, int64_t T, int64_t K, int64_t N, int64_t E, int dtype, int trans_b,
-                     int64_t tile_rows, int act, int grid_tiles, DeviceInfo* di, cudaStream_t stream) {
+                     int64_t tile_rows, int act, int grid_tiles, DeviceInfo* di, cudaStream_t stream,
+                     bool swap = false) {
   int rc = GMM_OK;
   cudaError_t ce;
   struct {
@@ -1038,6 +1074,13 @@ int setup_and_launch(GmmParams& prm, const void* A, const void* B, uint8_t* ws, 
 
   const int grid = std::max(1, std::min(pl.total_tiles, di->sm_count));
   if (dtype == GMM_DTYPE_F32) return launch_variant<kKindTf32x3, false>(prm, grid, stream, di, 0);
+  if (swap) {
+    if (dtype == GMM_DTYPE_BF16)
+      return trans_b ? launch_swap<kKindBf16, false>(prm, grid, stream, di, 11)
+                     : launch_swap<kKindBf16, true>(prm, grid, stream, di, 12);
+    return trans_b ? launch_swap<kKindF16, false>(prm, grid, stream, di, 13)
+                   : launch_swap<kKindF16, true>(prm, grid, stream, di, 14);
+  }
   if (tile_rows == 256) {
     if (dtype == GMM_DTYPE_BF16)
       return trans_b ? launch_pair<kKindBf16, false>(prm, pl.total_tiles, stream, di, 5)
@@ -1060,7 +1103,8 @@ int forward_impl(const void* A, const void* B, const int64_t* batch_sizes, int64
   Plan pl;
   int rc = make_plan(batch_sizes, num_experts, num_tokens, dim, dim_out, dtype, pl);
   if (rc != GMM_OK) return rc;
-  const int64_t tile_rows = choose_tile_rows(batch_sizes, num_experts, num_tokens, dtype);
+  const TileKind kind = choose_tile_kind(batch_sizes, num_experts, num_tokens, dtype, act, ep != nullptr);
+  const int64_t tile_rows = kind == kTilePair ? 256 : 128;
   if (tile_rows != 128 &&
       (rc = make_plan(batch_sizes, num_experts, num_tokens, dim, dim_out, dtype, pl, tile_rows)) != GMM_OK)
     return rc;
@@ -1120,6 +1164,7 @@ int forward_impl(const void* A, const void* B, const int64_t* batch_sizes, int64
   prm.dim_out = static_cast<int>(N_out);
   prm.act = act;
   prm.act_cols = act ? static_cast<int>(N_out) : 0;
+  prm.tile_rows = static_cast<int>(tile_rows);
   if (ep) {
     prm.remote = 1;
     prm.world = ep->world;
@@ -1138,7 +1183,7 @@ int forward_impl(const void* A, const void* B, const int64_t* batch_sizes, int64
   }
 
   return setup_and_launch(prm, A, B, ws, pl.a_part, pl.b_part, T, K, N, E, dtype, trans_b, tile_rows, act,
-                          pl.total_tiles, di, stream);
+                          pl.total_tiles, di, stream, kind == kTileSwap);
 }
 
 }  // namespace
@@ -1315,12 +1360,19 @@ int gmm_sm100_forward_dev(const void* A, const void* B, const int32_t* batch_siz
   const size_t need = gmm_sm100_dev_workspace_size(E, T, K, N, dtype);
   if (need > 0 && (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255u)))
     return fail(GMM_ERR_WORKSPACE, "workspace needs " + std::to_string(need) + " bytes (256-byte aligned)");
-  // Tile rows from the capacity alone (the sizes are only known on the device).
+  // Tile kind from the capacity alone (the sizes are only known on the device):
+  // CTA pairs when the capacity averages at least 384 rows per expert,
+  // swap-AB tiles when it averages at most 16 (decode), else 128-row tiles.
   int64_t tile_rows = 128;
+  bool swap = false;
   if (dtype != GMM_DTYPE_F32) {
     const char* force = std::getenv("GMM_SM100_TILE");
     if (force && std::strcmp(force, "256") == 0) tile_rows = 256;
-    else if (!(force && std::strcmp(force, "128") == 0)) tile_rows = T >= 384 * E ? 256 : 128;
+    else if (force && std::strcmp(force, "swap") == 0) swap = !swiglu;
+    else if (!(force && std::strcmp(force, "128") == 0)) {
+      if (T >= 384 * E) tile_rows = 256;
+      else swap = !swiglu && T <= 16 * E;
+    }
   }
   const int64_t BN = dtype == GMM_DTYPE_F32 ? 128 : 256;
   const int64_t BK = dtype == GMM_DTYPE_F32 ? 32 : 64;
@@ -1340,7 +1392,7 @@ int gmm_sm100_forward_dev(const void* A, const void* B, const int32_t* batch_siz
   const size_t a_part = dtype == GMM_DTYPE_F32 ? round_up(static_cast<size_t>(T) * K * 4, 256) : 0;
   const size_t b_part = dtype == GMM_DTYPE_F32 ? round_up(static_cast<size_t>(E) * K * N * 4, 256) : 0;
   return setup_and_launch(prm, A, B, static_cast<uint8_t*>(workspace), a_part, b_part, T, K, N, E, dtype,
-                          trans_b, tile_rows, prm.act, INT32_MAX, di, stream);
+                          trans_b, tile_rows, prm.act, INT32_MAX, di, stream, swap);
 }
 
 int gmm_sm100_forward_vark(const void* A, const void* B, const int64_t* batch_sizes, int64_t num_experts,

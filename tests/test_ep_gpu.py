@@ -25,9 +25,11 @@ def _free_port():
     return path
 
 
-def _worker(rank, world, port, E, dtype, trans_b, transport):
+def _worker(rank, world, port, E, dtype, trans_b, transport, tile):
     import sys
     sys.path.insert(0, ROOT)
+    if tile != "auto":  # the single-GPU op and the EP layer must run the same kernel family
+        os.environ["GMM_SM100_TILE"] = tile
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", init_method=f"file://{port}", rank=rank,
@@ -59,13 +61,14 @@ def _worker(rank, world, port, E, dtype, trans_b, transport):
 
 
 @pytest.mark.parametrize("transport", ["direct", "nccl"])
-@pytest.mark.parametrize("E,dtype,trans_b", [(8, torch.bfloat16, False), (16, torch.float16, True),
-                                             (8, torch.float32, False)])
-def test_ep_matches_single_gpu(E, dtype, trans_b, transport):
+@pytest.mark.parametrize("E,dtype,trans_b,tile", [(8, torch.bfloat16, False, "256"),
+                                                  (16, torch.float16, True, "128"),
+                                                  (8, torch.float32, False, "auto")])
+def test_ep_matches_single_gpu(E, dtype, trans_b, tile, transport):
     n = torch.cuda.device_count() if torch.cuda.is_available() else 0
     if n < 2:
         pytest.skip("needs 2 GPUs")
     world = min(n, 8)
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
-    mp.spawn(_worker, args=(world, _free_port(), E, dtype, trans_b, transport), nprocs=world,
+    mp.spawn(_worker, args=(world, _free_port(), E, dtype, trans_b, transport, tile), nprocs=world,
              join=True)

@@ -33,9 +33,11 @@ def _device():
     assert capi.device_error(clear=True) == 0, "a kernel recorded a device-side timeout"
 
 
-@pytest.fixture(params=["128", "256"])
+@pytest.fixture(params=["128", "256", "swap"])
 def tile(request, monkeypatch):
-    """Run a test with the single-CTA (128-row) or the CTA-pair (256-row) kernel forced."""
+    """Run a test with one kernel forced: single-CTA 128-row tiles, CTA-pair
+    256-row tiles, or swap-AB tiles (16-bit problems only; fp32 keeps its own
+    kernel)."""
     monkeypatch.setenv("GMM_SM100_TILE", request.param)
     return request.param
 
@@ -178,6 +180,8 @@ def _config_inputs(cid):
 
 @pytest.mark.parametrize("cid", [1, 2, 3, 4, 5])
 def test_config_parity(cid, tile):
+    if tile == "swap" and cid == 1:
+        pytest.skip("fp32 has no swap-AB kernel")
     cfg, bs, a, b = _config_inputs(cid)
     out = _fwd(a, b, bs, cfg.trans_b)
     torch.cuda.synchronize()
@@ -230,3 +234,27 @@ def test_host_streamed_matches_device_op(dtype, trans_b):
         got = hopper_gmm_fwd_host(a, b, bs, trans_b=trans_b)
         torch.cuda.synchronize()
         assert torch.equal(got, want)
+
+
+def test_default_swap_tiles_match_the_128_row_kernel_and_the_oracle(monkeypatch):
+    """Decode-shaped routing (small experts) takes swap-AB tiles by default;
+    their output must agree with the 128-row kernel and the oracle."""
+    monkeypatch.delenv("GMM_SM100_TILE", raising=False)
+    g = torch.Generator().manual_seed(21)
+    bs = torch.randint(0, 17, (96,), generator=g)
+    bs[::5] = 0
+    bs[7] = 64
+    T, dim, dim_out = int(bs.sum()), 384, 1000
+    for dtype, trans_b in ((torch.bfloat16, False), (torch.float16, True)):
+        a = torch.randn(T, dim, generator=g).to(dtype)
+        shape = (len(bs), dim_out, dim) if trans_b else (len(bs), dim, dim_out)
+        b = (torch.randn(*shape, generator=g) / dim ** 0.5).to(dtype)
+        auto = _fwd(a.cuda(), b.cuda(), bs, trans_b).cpu()
+        monkeypatch.setenv("GMM_SM100_TILE", "128")
+        big = _fwd(a.cuda(), b.cuda(), bs, trans_b).cpu()
+        monkeypatch.delenv("GMM_SM100_TILE")
+        name = oracle.dtype_name(dtype)
+        want = oracle.round_to(oracle.gmm_oracle_c(a, b, bs, trans_b), name)
+        for got in (auto, big):
+            ok, nbad, err = oracle.allclose_report(got.float().numpy(), want, oracle.TOLERANCE[name])
+            assert ok, (name, nbad, err)

@@ -22,7 +22,7 @@ def _device():
     torch.cuda.set_device(0)
 
 
-@pytest.fixture(params=["128", "256"])
+@pytest.fixture(params=["128", "256", "swap"])
 def tile(request, monkeypatch):
     monkeypatch.setenv("GMM_SM100_TILE", request.param)
     return request.param

@@ -24,7 +24,7 @@ def _device():
     capi.device_error(clear=True)
 
 
-@pytest.fixture(params=["128", "256"])
+@pytest.fixture(params=["128", "256", "swap"])
 def tile(request, monkeypatch):
     monkeypatch.setenv("GMM_SM100_TILE", request.param)
     return request.param
