@@ -108,3 +108,44 @@ def test_swiglu_op_schema_and_fake():
         b = torch.empty(2, 32, 96, dtype=torch.bfloat16, device="cuda")
         out = gmm_b200.gmm_swiglu(a, b, torch.tensor([30, 34]))
         assert tuple(out.shape) == (64, 48)
+
+
+def test_cabi_other_entries_validate_on_host():
+    """Every entry point rejects bad arguments with a status and a message
+    before it touches the GPU (dummy non-null pointers, no device here)."""
+    from gmm_b200 import capi
+    lib = capi.load()
+    P = 256  # a non-null, 16-byte-aligned dummy address; never dereferenced
+
+    def last():
+        return lib.gmm_sm100_last_error().decode()
+
+    bs = np.asarray([3, 4], dtype=np.int64)
+    # variable-K: sum, dtype, row pitch
+    assert lib.gmm_sm100_forward_vark(P, P, bs.ctypes.data, 2, 9, 64, 64, 1, P, None) == -2
+    assert "Sum of batch_sizes (7)" in last()
+    assert lib.gmm_sm100_forward_vark(P, P, bs.ctypes.data, 2, 7, 64, 64, 0, P, None) == -3
+    assert lib.gmm_sm100_forward_vark(P, P, bs.ctypes.data, 2, 7, 12, 64, 1, P, None) == -4
+    # SwiGLU: 16-bit only, gate/up width a multiple of 8
+    assert lib.gmm_sm100_forward_swiglu(P, P, bs.ctypes.data, 2, 7, 64, 128, 0, 0, P, None, 0, None) == -3
+    assert lib.gmm_sm100_forward_swiglu(P, P, bs.ctypes.data, 2, 7, 64, 40, 1, 0, P, None, 0, None) == -4
+    # device batch sizes: expert count, SwiGLU dtype, alignment of D and of the sizes
+    assert lib.gmm_sm100_forward_dev(P, P, P, 0, 8, 64, 64, 1, 0, 0, P, None, 0, None) == -1
+    assert lib.gmm_sm100_forward_dev(P, P, P, 1025, 8, 64, 64, 1, 0, 0, P, None, 0, None) == -1
+    assert lib.gmm_sm100_forward_dev(P, P, P, 4, 8, 64, 64, 0, 0, 1, P, None, 0, None) == -1
+    assert lib.gmm_sm100_forward_dev(P, P, P, 4, 8, 64, 64, 1, 0, 0, P + 8, None, 0, None) == -4
+    assert lib.gmm_sm100_forward_dev(P, P, P + 2, 4, 8, 64, 64, 1, 0, 0, P, None, 0, None) == -4
+    # the allocation-free fp32 entry: a problem whose scratch exceeds the fixed array
+    big = np.asarray([1024], dtype=np.int64)
+    rc = lib.gmm_sm100_forward_f32_noalloc(P, P, big.ctypes.data, 1, 1024, 1024, 1024, 0, P, None)
+    assert rc == -8 and "fixed scratch holds 8388608 bytes" in last()
+    assert lib.gmm_sm100_forward_f32_noalloc(P, P, bs.ctypes.data, 2, 9, 64, 64, 0, P, None) == -2
+    # routing and permutation
+    moe_last = lambda: lib.gmm_sm100_moe_last_error().decode()  # noqa: E731
+    assert lib.gmm_sm100_moe_topk(P, 0, 16, 8, 0, 1, P, P, None) == -1
+    assert lib.gmm_sm100_moe_topk(P, 0, 16, 8, 9, 1, P, P, None) == -1
+    assert lib.gmm_sm100_moe_topk(P, 0, 16, 2000, 2, 1, P, P, None) == -1 and "1024" in moe_last()
+    assert lib.gmm_sm100_moe_permute(P, 16, 24, P, 2, 8, P, P, P, P, None, 0, None) == -4
+    assert lib.gmm_sm100_moe_permute(P, 16, 32, P, 2, 0, P, P, P, P, None, 0, None) == -1
+    assert lib.gmm_sm100_moe_unpermute(P, P, P, 16, 2, 12, 1, P, None) == -4
+    assert lib.gmm_sm100_moe_unpermute(P, P, P, 16, 0, 64, 1, P, None) == -1
