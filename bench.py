@@ -209,7 +209,7 @@ def run_single(args):
         a, b = make_inputs(cfg, "cuda")
     flops = cfg.flops()
     alg_bytes = cfg.algorithmic_bytes(bs)
-    launches_per_step = 3 if cfg.dtype == torch.float32 else 1
+    launches_per_step = 2 if cfg.dtype == torch.float32 else 1  # fp32: split pre-pass + GEMM
 
     stream = torch.cuda.current_stream()
     for _ in range(max(3, args.warmup)):

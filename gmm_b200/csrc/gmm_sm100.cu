@@ -653,41 +653,73 @@ __device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
   }
 }
 
-__global__ void split_tf32_kernel(const float4* __restrict__ x, float4* __restrict__ hi,
-                                  float4* __restrict__ lo, long long n4) {
-  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n4;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const float4 v = x[i];
-    float4 h, l;
-    split_tf32(v.x, h.x, l.x);
-    split_tf32(v.y, h.y, l.y);
-    split_tf32(v.z, h.z, l.z);
-    split_tf32(v.w, h.w, l.w);
-    hi[i] = h;
-    lo[i] = l;
-  }
+__device__ __forceinline__ void split_tf32_vec(const float4* __restrict__ x, float4* __restrict__ hi,
+                                               float4* __restrict__ lo, long long i) {
+  const float4 v = x[i];
+  float4 h, l;
+  split_tf32(v.x, h.x, l.x);
+  split_tf32(v.y, h.y, l.y);
+  split_tf32(v.z, h.z, l.z);
+  split_tf32(v.w, h.w, l.w);
+  hi[i] = h;
+  lo[i] = l;
 }
 
-// b[e] is [K, N]; writes hi[e], lo[e] as [N, K] (K contiguous) for K-major TF32 operands.
-__global__ void split_tf32_transpose_kernel(const float* __restrict__ b, float* __restrict__ hi,
-                                            float* __restrict__ lo, int K, int N) {
-  __shared__ float tile[32][33];
-  const long long e_off = static_cast<long long>(blockIdx.z) * K * N;
-  const int n0 = blockIdx.x * 32, k0 = blockIdx.y * 32;
-  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-    const int k = k0 + i, n = n0 + threadIdx.x;
-    tile[i][threadIdx.x] = (k < K && n < N) ? b[e_off + static_cast<long long>(k) * N + n] : 0.f;
+struct SplitArgs {
+  const float4* a;
+  float4* a_hi;
+  float4* a_lo;
+  long long n4a;  // float4s of A
+  int a_blocks;   // blocks [0, a_blocks) split A; the rest split B
+  const float* b;
+  float* b_hi;
+  float* b_lo;
+  long long n4b;  // float4s of B (trans_b)
+  int K, N, trans_b;
+  int nt_n, nt_k;       // 32x32 tiles of one B[e] (transposing split)
+  long long b_tiles;    // E * nt_n * nt_k
+};
+
+// The whole fp32 pre-pass in one launch: A (and a K-major B) split element by
+// element; a [K, N] B split while transposed to [N, K] (K contiguous) through
+// 32x32 shared-memory tiles, for the K-major TF32 operands of the GEMM.
+__global__ void __launch_bounds__(256) split_operands_kernel(const SplitArgs sa) {
+  if (static_cast<int>(blockIdx.x) < sa.a_blocks) {
+    for (long long i = blockIdx.x * 256LL + threadIdx.x; i < sa.n4a; i += sa.a_blocks * 256LL)
+      split_tf32_vec(sa.a, sa.a_hi, sa.a_lo, i);
+    return;
   }
-  __syncthreads();
-  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-    const int n = n0 + i, k = k0 + threadIdx.x;
-    if (n < N && k < K) {
-      float h, l;
-      split_tf32(tile[threadIdx.x][i], h, l);
-      const long long o = e_off + static_cast<long long>(n) * K + k;
-      hi[o] = h;
-      lo[o] = l;
+  const long long bb = blockIdx.x - sa.a_blocks, nb = gridDim.x - sa.a_blocks;
+  if (sa.trans_b) {
+    const float4* b4 = reinterpret_cast<const float4*>(sa.b);
+    for (long long i = bb * 256 + threadIdx.x; i < sa.n4b; i += nb * 256)
+      split_tf32_vec(b4, reinterpret_cast<float4*>(sa.b_hi), reinterpret_cast<float4*>(sa.b_lo), i);
+    return;
+  }
+  __shared__ float tile[32][33];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8 threads
+  const long long per_e = static_cast<long long>(sa.nt_n) * sa.nt_k;
+  for (long long t = bb; t < sa.b_tiles; t += nb) {
+    const long long e = t / per_e;
+    const int r = static_cast<int>(t - e * per_e);
+    const int k0 = (r / sa.nt_n) * 32, n0 = (r % sa.nt_n) * 32;
+    const long long e_off = e * sa.K * sa.N;
+    for (int i = ty; i < 32; i += 8) {
+      const int k = k0 + i, n = n0 + tx;
+      tile[i][tx] = (k < sa.K && n < sa.N) ? sa.b[e_off + static_cast<long long>(k) * sa.N + n] : 0.f;
     }
+    __syncthreads();
+    for (int i = ty; i < 32; i += 8) {
+      const int n = n0 + i, k = k0 + tx;
+      if (n < sa.N && k < sa.K) {
+        float h, l;
+        split_tf32(tile[tx][i], h, l);
+        const long long o = e_off + static_cast<long long>(n) * sa.K + k;
+        sa.b_hi[o] = h;
+        sa.b_lo[o] = l;
+      }
+    }
+    __syncthreads();
   }
 }
 
@@ -1011,6 +1043,34 @@ bool append_ep_table(Plan& pl, const int64_t* local_bs, int64_t E, const EpRoute
   return true;
 }
 
+// The fp32 pre-pass (one launch): hi/lo splits of A into a_hi/a_lo and of B,
+// K-major, into b_hi/b_lo.
+int launch_split(const void* A, const void* B, float* a_hi, float* a_lo, float* b_hi, float* b_lo, int64_t T,
+                 int64_t K, int64_t N, int64_t E, int trans_b, int sm_count, cudaStream_t stream) {
+  SplitArgs sa;
+  sa.a = reinterpret_cast<const float4*>(A);
+  sa.a_hi = reinterpret_cast<float4*>(a_hi);
+  sa.a_lo = reinterpret_cast<float4*>(a_lo);
+  sa.n4a = T * K / 4;
+  sa.a_blocks = static_cast<int>(std::max<long long>(1, std::min<long long>((sa.n4a + 255) / 256, 4LL * sm_count)));
+  sa.b = static_cast<const float*>(B);
+  sa.b_hi = b_hi;
+  sa.b_lo = b_lo;
+  sa.n4b = E * K * N / 4;
+  sa.K = static_cast<int>(K);
+  sa.N = static_cast<int>(N);
+  sa.trans_b = trans_b ? 1 : 0;
+  sa.nt_n = static_cast<int>((N + 31) / 32);
+  sa.nt_k = static_cast<int>((K + 31) / 32);
+  sa.b_tiles = E * sa.nt_n * static_cast<long long>(sa.nt_k);
+  const long long b_blocks = std::max<long long>(
+      1, trans_b ? std::min<long long>((sa.n4b + 255) / 256, 4LL * sm_count)
+                 : std::min<long long>(sa.b_tiles, 16LL * sm_count));
+  split_operands_kernel<<<static_cast<unsigned>(sa.a_blocks + b_blocks), 256, 0, stream>>>(sa);
+  cudaError_t ce = cudaGetLastError();
+  return ce == cudaSuccess ? GMM_OK : cuda_fail(ce, "split pre-pass launch");
+}
+
 // Operand preparation (fp32 hi/lo split pre-pass, tensor maps) and the
 // launch of the chosen kernel variant.  `grid_tiles` caps the grid (the tile
 // count when the host knows it).
@@ -1019,7 +1079,6 @@ int setup_and_launch(GmmParams& prm, const void* A, const void* B, uint8_t* ws, 
                      int64_t tile_rows, int act, int grid_tiles, DeviceInfo* di, cudaStream_t stream,
                      bool swap = false) {
   int rc = GMM_OK;
-  cudaError_t ce;
   struct {
     size_t a_part, b_part, split_bytes;
     int total_tiles;
@@ -1030,22 +1089,7 @@ int setup_and_launch(GmmParams& prm, const void* A, const void* B, uint8_t* ws, 
     float* a_lo = reinterpret_cast<float*>(ws + pl.a_part);
     float* b_hi = reinterpret_cast<float*>(ws + 2 * pl.a_part);
     float* b_lo = reinterpret_cast<float*>(ws + 2 * pl.a_part + pl.b_part);
-    const long long n4a = T * K / 4;
-    const int sgrid = static_cast<int>(std::min<long long>((n4a + 255) / 256, 4LL * di->sm_count));
-    split_tf32_kernel<<<std::max(sgrid, 1), 256, 0, stream>>>(
-        reinterpret_cast<const float4*>(A), reinterpret_cast<float4*>(a_hi), reinterpret_cast<float4*>(a_lo), n4a);
-    if (trans_b) {
-      const long long n4b = E * K * N / 4;
-      const int bgrid = static_cast<int>(std::min<long long>((n4b + 255) / 256, 4LL * di->sm_count));
-      split_tf32_kernel<<<std::max(bgrid, 1), 256, 0, stream>>>(
-          reinterpret_cast<const float4*>(B), reinterpret_cast<float4*>(b_hi), reinterpret_cast<float4*>(b_lo), n4b);
-    } else {
-      dim3 tg(static_cast<unsigned>((N + 31) / 32), static_cast<unsigned>((K + 31) / 32), static_cast<unsigned>(E));
-      split_tf32_transpose_kernel<<<tg, dim3(32, 8), 0, stream>>>(static_cast<const float*>(B), b_hi, b_lo,
-                                                                  static_cast<int>(K), static_cast<int>(N));
-    }
-    ce = cudaGetLastError();
-    if (ce != cudaSuccess) return cuda_fail(ce, "split pre-pass launch");
+    if ((rc = launch_split(A, B, a_hi, a_lo, b_hi, b_lo, T, K, N, E, trans_b, di->sm_count, stream))) return rc;
     const cuuint64_t adims[2] = {uK, uT}, astr[1] = {uK * 4};
     const cuuint32_t abox[2] = {32, 128};
     const cuuint64_t bdims[3] = {uK, uN, uE}, bstr[2] = {uK * 4, uN * uK * 4};
@@ -1577,21 +1621,7 @@ extern "C" int gmm_sm100_forward_f32_noalloc(const float* A, const float* B,
   float* a_lo = reinterpret_cast<float*>(ws + pl.a_part);
   float* b_hi = reinterpret_cast<float*>(ws + 2 * pl.a_part);
   float* b_lo = reinterpret_cast<float*>(ws + 2 * pl.a_part + pl.b_part);
-  const long long n4a = T * K / 4;
-  const int sgrid = static_cast<int>(std::min<long long>((n4a + 255) / 256, 4LL * di->sm_count));
-  split_tf32_kernel<<<std::max(sgrid, 1), 256, 0, stream>>>(
-      reinterpret_cast<const float4*>(A), reinterpret_cast<float4*>(a_hi), reinterpret_cast<float4*>(a_lo), n4a);
-  if (trans_b) {
-    const long long n4b = E * K * N / 4;
-    const int bgrid = static_cast<int>(std::min<long long>((n4b + 255) / 256, 4LL * di->sm_count));
-    split_tf32_kernel<<<std::max(bgrid, 1), 256, 0, stream>>>(
-        reinterpret_cast<const float4*>(B), reinterpret_cast<float4*>(b_hi), reinterpret_cast<float4*>(b_lo), n4b);
-  } else {
-    dim3 tg(static_cast<unsigned>((N + 31) / 32), static_cast<unsigned>((K + 31) / 32), static_cast<unsigned>(E));
-    split_tf32_transpose_kernel<<<tg, dim3(32, 8), 0, stream>>>(B, b_hi, b_lo, static_cast<int>(K), static_cast<int>(N));
-  }
-  ce = cudaGetLastError();
-  if (ce != cudaSuccess) return cuda_fail(ce, "split pre-pass launch");
+  if ((rc = launch_split(A, B, a_hi, a_lo, b_hi, b_lo, T, K, N, E, trans_b, di->sm_count, stream))) return rc;
   const cuuint64_t uT = T, uK = K, uN = N, uE = E;
   const cuuint64_t adims[2] = {uK, uT}, astr[1] = {uK * 4};
   const cuuint32_t abox[2] = {32, 128};
