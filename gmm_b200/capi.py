@@ -69,6 +69,14 @@ _SIGNATURES = {
     "gmm_sm100_ep_workspace_size": (ctypes.c_size_t, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int,
                                                       ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                                       ctypes.c_int]),
+    "gmm_sm100_plan": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                      ctypes.c_int64, ctypes.c_int, ctypes.c_int,
+                                      ctypes.POINTER(ctypes.c_void_p)]),
+    "gmm_sm100_plan_workspace_size": (ctypes.c_size_t, [ctypes.c_void_p]),
+    "gmm_sm100_launch": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
+                                        ctypes.c_void_p]),
+    "gmm_sm100_plan_free": (None, [ctypes.c_void_p]),
     "gmm_sm100_forward_f32_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p,
                                                      ctypes.c_void_p, ctypes.c_int64,
                                                      ctypes.c_int64, ctypes.c_int64,
@@ -135,6 +143,40 @@ def forward(a, b, batch_sizes, d, trans_b=False, workspace=None, stream=None):
                                     a.shape[0], dim, dim_out, dtype, int(bool(trans_b)),
                                     d.data_ptr(), workspace.data_ptr() if need else None, need, s))
     return d
+
+
+class Plan:
+    """``gmm_sm100_plan``: the host half of a grouped GEMM (tile table, kernel
+    choice), built once from host batch sizes and launched any number of times
+    on operands of its shapes with ``launch`` (``gmm_sm100_launch``)."""
+
+    def __init__(self, batch_sizes, num_tokens, dim, dim_out, dtype, trans_b=False):
+        import numpy as np
+        bs = np.ascontiguousarray(np.asarray(batch_sizes, dtype=np.int64))
+        self._lib = load()
+        handle = ctypes.c_void_p()
+        _check(self._lib.gmm_sm100_plan(bs.ctypes.data, bs.shape[0], num_tokens, dim, dim_out, dtype,
+                                        int(bool(trans_b)), ctypes.byref(handle)))
+        self._h = handle.value
+        self.workspace_size = int(self._lib.gmm_sm100_plan_workspace_size(self._h))
+
+    def launch(self, a, b, d, workspace=None, stream=None):
+        import torch
+        need = self.workspace_size
+        if need and workspace is None:
+            workspace = torch.empty(need, dtype=torch.uint8, device=a.device)
+        s = torch.cuda.current_stream(a.device).cuda_stream if stream is None else stream
+        _check(self._lib.gmm_sm100_launch(self._h, a.data_ptr(), b.data_ptr(), d.data_ptr(),
+                                          workspace.data_ptr() if need else None, need, s))
+        return d
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self._lib.gmm_sm100_plan_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
 
 
 def device_error(clear=True) -> int:

@@ -31,6 +31,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <memory>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -1139,20 +1140,44 @@ int setup_and_launch(GmmParams& prm, const void* A, const void* B, uint8_t* ws, 
                  : launch_variant<kKindF16, true>(prm, grid, stream, di, 4);
 }
 
-int forward_impl(const void* A, const void* B, const int64_t* batch_sizes, int64_t num_experts,
-                 int64_t num_tokens, int64_t dim, int64_t dim_out, int dtype, int trans_b, void* D,
-                 void* workspace, size_t workspace_bytes, void* stream_ptr, const EpRoute* ep,
-                 int act = 0) {
-  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+// The host half of a forward call: the tile table and the kernel choice,
+// from the host batch sizes alone (no CUDA call).
+struct PlanObj {
   Plan pl;
-  int rc = make_plan(batch_sizes, num_experts, num_tokens, dim, dim_out, dtype, pl);
+  TileKind kind = kTile128;
+  int64_t tile_rows = 128;
+  int64_t E = 0, T = 0, K = 0, N = 0;
+  int dtype = 0, trans_b = 0;
+};
+
+int plan_impl(const int64_t* batch_sizes, int64_t num_experts, int64_t num_tokens, int64_t dim,
+              int64_t dim_out, int dtype, int trans_b, int act, bool remote, PlanObj& po) {
+  int rc = make_plan(batch_sizes, num_experts, num_tokens, dim, dim_out, dtype, po.pl);
   if (rc != GMM_OK) return rc;
-  const TileKind kind = choose_tile_kind(batch_sizes, num_experts, num_tokens, dtype, act, ep != nullptr);
-  const int64_t tile_rows = kind == kTilePair ? 256 : 128;
-  if (tile_rows != 128 &&
-      (rc = make_plan(batch_sizes, num_experts, num_tokens, dim, dim_out, dtype, pl, tile_rows)) != GMM_OK)
+  po.kind = choose_tile_kind(batch_sizes, num_experts, num_tokens, dtype, act, remote);
+  po.tile_rows = po.kind == kTilePair ? 256 : 128;
+  if (po.tile_rows != 128 &&
+      (rc = make_plan(batch_sizes, num_experts, num_tokens, dim, dim_out, dtype, po.pl, po.tile_rows)) != GMM_OK)
     return rc;
-  const int64_t T = num_tokens, K = dim, N = dim_out, E = num_experts;
+  po.E = num_experts;
+  po.T = num_tokens;
+  po.K = dim;
+  po.N = dim_out;
+  po.dtype = dtype;
+  po.trans_b = trans_b;
+  return GMM_OK;
+}
+
+// The device half: argument checks that need the pointers, tensor maps, launch.
+// `pl` is the plan's table (with the expert-parallel segments appended in EP mode).
+int launch_impl(const PlanObj& po, const Plan& pl, const void* A, const void* B, void* D, void* workspace,
+                size_t workspace_bytes, void* stream_ptr, const EpRoute* ep, int act) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  int rc = GMM_OK;
+  const TileKind kind = po.kind;
+  const int64_t tile_rows = po.tile_rows;
+  const int64_t T = po.T, K = po.K, N = po.N, E = po.E;
+  const int dtype = po.dtype, trans_b = po.trans_b;
   if (T == 0 || N == 0) return GMM_OK;  // nothing to write
   const int es = elem_size(dtype);
   // SwiGLU: B has 2*I output columns ([gate | up]); D has I = N / 2 columns.
@@ -1169,7 +1194,6 @@ int forward_impl(const void* A, const void* B, const int64_t* batch_sizes, int64
       if (!ep->out_peers[s] || !aligned16(ep->out_peers[s]))
         return fail(GMM_ERR_ALIGNMENT, "every rank's output buffer must be non-null and 16-byte aligned");
     if (K == 0) return fail(GMM_ERR_INVALID_ARGUMENT, "expert-parallel forward needs dim > 0");
-    if (!append_ep_table(pl, batch_sizes, E, *ep)) return fail(GMM_ERR_TOO_LARGE, "EP table too large");
   } else {
     if (!D) return fail(GMM_ERR_INVALID_ARGUMENT, "D is null");
     if (!aligned16(D)) return fail(GMM_ERR_ALIGNMENT, "D must be 16-byte aligned");
@@ -1230,7 +1254,24 @@ int forward_impl(const void* A, const void* B, const int64_t* batch_sizes, int64
                           pl.total_tiles, di, stream, kind == kTileSwap);
 }
 
+int forward_impl(const void* A, const void* B, const int64_t* batch_sizes, int64_t num_experts,
+                 int64_t num_tokens, int64_t dim, int64_t dim_out, int dtype, int trans_b, void* D,
+                 void* workspace, size_t workspace_bytes, void* stream_ptr, const EpRoute* ep,
+                 int act = 0) {
+  PlanObj po;
+  int rc = plan_impl(batch_sizes, num_experts, num_tokens, dim, dim_out, dtype, trans_b, act, ep != nullptr, po);
+  if (rc != GMM_OK) return rc;
+  if (ep && num_tokens > 0 && dim_out > 0 && ep->world >= 1 && ep->world <= kMaxPeers &&
+      !append_ep_table(po.pl, batch_sizes, num_experts, *ep))
+    return fail(GMM_ERR_TOO_LARGE, "EP table too large");
+  return launch_impl(po, po.pl, A, B, D, workspace, workspace_bytes, stream_ptr, ep, act);
+}
+
 }  // namespace
+
+struct gmm_sm100_plan_s {
+  PlanObj po;
+};
 
 extern "C" {
 
@@ -1271,6 +1312,33 @@ int gmm_sm100_forward(const void* A, const void* B, const int64_t* batch_sizes, 
   return forward_impl(A, B, batch_sizes, num_experts, num_tokens, dim, dim_out, dtype, trans_b, D,
                       workspace, workspace_bytes, stream_ptr, nullptr);
 }
+
+int gmm_sm100_plan(const int64_t* batch_sizes, int64_t num_experts, int64_t num_tokens, int64_t dim,
+                   int64_t dim_out, int dtype, int trans_b, gmm_sm100_plan_t** plan_out) {
+  if (!plan_out) return fail(GMM_ERR_INVALID_ARGUMENT, "plan_out is null");
+  *plan_out = nullptr;
+  try {
+    std::unique_ptr<gmm_sm100_plan_s> h(new gmm_sm100_plan_s);
+    const int rc = plan_impl(batch_sizes, num_experts, num_tokens, dim, dim_out, dtype, trans_b, 0, false, h->po);
+    if (rc != GMM_OK) return rc;
+    *plan_out = h.release();
+    return GMM_OK;
+  } catch (const std::exception& e) {
+    return fail(GMM_ERR_TOO_LARGE, std::string("host allocation failed: ") + e.what());
+  }
+}
+
+size_t gmm_sm100_plan_workspace_size(const gmm_sm100_plan_t* plan) {
+  return plan ? plan->po.pl.split_bytes + plan->po.pl.table_bytes : 0;
+}
+
+int gmm_sm100_launch(const gmm_sm100_plan_t* plan, const void* A, const void* B, void* D, void* workspace,
+                     size_t workspace_bytes, void* stream) {
+  if (!plan) return fail(GMM_ERR_INVALID_ARGUMENT, "plan is null");
+  return launch_impl(plan->po, plan->po.pl, A, B, D, workspace, workspace_bytes, stream, nullptr, 0);
+}
+
+void gmm_sm100_plan_free(gmm_sm100_plan_t* plan) { delete plan; }
 
 size_t gmm_sm100_ep_workspace_size(const int64_t* counts, int64_t num_local_experts, int world,
                                    int64_t num_rows, int64_t dim, int64_t dim_out, int dtype) {

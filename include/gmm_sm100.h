@@ -82,6 +82,26 @@ int gmm_sm100_forward(const void* A, const void* B, const int64_t* batch_sizes,
                       int dtype, int trans_b, void* D, void* workspace, size_t workspace_bytes,
                       void* stream);
 
+/* The same forward in two steps.  gmm_sm100_plan does the host half of
+ * gmm_sm100_forward -- validation, the tile table and the kernel choice from
+ * the host batch_sizes -- without any CUDA call; gmm_sm100_launch does the
+ * device half on given operands.  A plan is built once per routing and can be
+ * launched for every GEMM that shares the batch sizes (a layer's gate/up and
+ * down projections), from any thread and stream at once (it is never
+ * modified after creation).  Replaces the reference's host-side problem
+ * building, done again on every call (reference csrc/hopper_gmm_forward.cu:
+ * 230-316 CutlassGroupedGemm, :454-471 segmentation).  The GMM_SM100_TILE
+ * kernel override is read when the plan is made. */
+typedef struct gmm_sm100_plan_s gmm_sm100_plan_t;
+int gmm_sm100_plan(const int64_t* batch_sizes, int64_t num_experts, int64_t num_tokens, int64_t dim,
+                   int64_t dim_out, int dtype, int trans_b, gmm_sm100_plan_t** plan_out);
+/* Workspace bytes gmm_sm100_launch needs for this plan (0 for most 16-bit plans). */
+size_t gmm_sm100_plan_workspace_size(const gmm_sm100_plan_t* plan);
+/* A, B, D as in gmm_sm100_forward, with the plan's shapes and dtype. */
+int gmm_sm100_launch(const gmm_sm100_plan_t* plan, const void* A, const void* B, void* D, void* workspace,
+                     size_t workspace_bytes, void* stream);
+void gmm_sm100_plan_free(gmm_sm100_plan_t* plan);
+
 /* Fused MoE gate/up projection with SwiGLU.  No reference counterpart: the
  * reference stops at the grouped GEMM, and its MoE layer would call it twice
  * (gate+up, then down) with the activation in between.  B holds each

@@ -149,3 +149,33 @@ def test_cabi_other_entries_validate_on_host():
     assert lib.gmm_sm100_moe_permute(P, 16, 32, P, 2, 0, P, P, P, P, None, 0, None) == -1
     assert lib.gmm_sm100_moe_unpermute(P, P, P, 16, 2, 12, 1, P, None) == -4
     assert lib.gmm_sm100_moe_unpermute(P, P, P, 16, 0, 64, 1, P, None) == -1
+
+
+def test_plan_is_host_only_and_agrees_with_workspace_size():
+    """gmm_sm100_plan makes no CUDA call (this host has no GPU) and asks for
+    the workspace gmm_sm100_workspace_size reports for the same problem."""
+    import ctypes
+    from gmm_b200 import capi
+    lib = capi.load()
+    cases = [([64] * 8, 512, 128, 256, capi.GMM_DTYPE_F32, False),
+             ([5, 0, 300, 1], 306, 64, 128, capi.GMM_DTYPE_BF16, False),
+             ([2000] * 8, 16000, 64, 64, capi.GMM_DTYPE_BF16, True),
+             ([1] * 2000, 2000, 64, 64, capi.GMM_DTYPE_F16, True)]
+    for bs, T, dim, dim_out, dt, tb in cases:
+        p = capi.Plan(bs, T, dim, dim_out, dt, tb)
+        assert p.workspace_size == capi.workspace_size(bs, T, dim, dim_out, dt, tb)
+        p.close()
+    with pytest.raises(capi.GmmError, match=r"Sum of batch_sizes \(7\) must equal A.size\(0\) \(9\)"):
+        capi.Plan([3, 4], 9, 64, 64, capi.GMM_DTYPE_BF16)
+    with pytest.raises(capi.GmmError, match="Unsupported dtype"):
+        capi.Plan([3, 4], 7, 64, 64, 9)
+    arr = np.asarray([1, 2], dtype=np.int64)
+    assert lib.gmm_sm100_plan(arr.ctypes.data, 2, 3, 64, 64, 1, 0, None) == -1
+    assert lib.gmm_sm100_launch(None, 16, 16, 16, None, 0, None) == -1
+    # an empty problem launches as a no-op, without touching the device
+    h = ctypes.c_void_p()
+    zero = np.zeros(3, dtype=np.int64)
+    assert lib.gmm_sm100_plan(zero.ctypes.data, 3, 0, 64, 64, 1, 0, ctypes.byref(h)) == 0
+    assert lib.gmm_sm100_launch(h, 16, 16, 16, None, 0, None) == 0
+    lib.gmm_sm100_plan_free(h)
+    lib.gmm_sm100_plan_free(None)

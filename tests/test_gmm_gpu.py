@@ -258,3 +258,24 @@ def test_default_swap_tiles_match_the_128_row_kernel_and_the_oracle(monkeypatch)
         for got in (auto, big):
             ok, nbad, err = oracle.allclose_report(got.float().numpy(), want, oracle.TOLERANCE[name])
             assert ok, (name, nbad, err)
+
+
+@pytest.mark.parametrize("dtype,trans_b", [(torch.bfloat16, False), (torch.float16, True),
+                                           (torch.float32, False), (torch.bfloat16, True)])
+def test_plan_then_launch_matches_forward(dtype, trans_b):
+    """gmm_sm100_plan once, gmm_sm100_launch on two operand sets (two GEMMs that
+    share the routing): each bit-identical to a gmm_sm100_forward call."""
+    from gmm_b200 import capi
+    bs = [130, 0, 1, 700, 64, 0, 255, 9]
+    T, dim, dim_out = sum(bs), 192, 320
+    plan = capi.Plan(bs, T, dim, dim_out, capi.dtype_code(dtype), trans_b)
+    g = torch.Generator().manual_seed(41)
+    shape = (len(bs), dim_out, dim) if trans_b else (len(bs), dim, dim_out)
+    for _ in range(2):
+        a = torch.randn(T, dim, generator=g).to(dtype).cuda()
+        b = (torch.randn(*shape, generator=g) / dim ** 0.5).to(dtype).cuda()
+        got = plan.launch(a, b, torch.empty(T, dim_out, dtype=dtype, device="cuda"))
+        want = capi.forward(a, b, bs, torch.empty(T, dim_out, dtype=dtype, device="cuda"), trans_b=trans_b)
+        torch.cuda.synchronize()
+        assert torch.equal(got, want)
+    plan.close()
