@@ -15,9 +15,11 @@
 //     output type and store rows that belong to the tile's expert -- rows past
 //     an expert's segment are never written, which keeps output placement exact.
 //
-// bf16/fp16 problems whose experts are small or ragged go to the swap-AB
-// kernel of gmm_swap_kernel.cuh instead (output columns on the MMA's M,
-// token rows on its N, row blocks sized to the expert).
+// Two more kernels share the tile table: CTA pairs with 256-row tiles
+// (gmm_pair_kernel.cuh) when the non-empty experts average at least 384 rows,
+// and swap-AB tiles (gmm_swap_kernel.cuh: output columns on the MMA's M,
+// token rows on its N) for decode-shaped problems whose experts all have at
+// most 64 rows (choose_tile_kind).
 //
 // A is addressed through one 2D tensor map over all T rows (a tile of expert
 // g starts at row off_g + 128 m); B through one 3D tensor map whose outer
