@@ -163,10 +163,11 @@ def run(args, metric, load_peaks, clock_sampler):
                            "rows": int(rows_all.item()), "trans_b": cfg.trans_b,
                            "parallelism": f"ep{world}",
                            "l2": "inputs larger than L2 (126 MB)",
-                           "exchange": ("gloo count all-gather; NVLink peer-load gather + combine "
-                                        "fused into the GEMM epilogue (symmetric memory)")
-                           if ep._use_direct(b_local) else
-                           "gloo count all-gather + NCCL P2P dispatch/combine"},
+                           "exchange": (("shared-memory" if ep._shm_counts is not None else "gloo")
+                                        + " count all-gather; "
+                                        + ("NVLink peer-load gather + combine fused into the GEMM "
+                                           "epilogue (symmetric memory)" if ep._use_direct(b_local)
+                                           else "NCCL P2P dispatch/combine"))},
                 "e2e": {"value": round(flops / (ems.item() * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
                         "ms_per_step": round(ems.item(), 3),
                         "h2d_bytes_per_step": int(h2d.item()), "d2h_bytes_per_step": int(d2h.item()),
