@@ -279,3 +279,42 @@ def test_plan_then_launch_matches_forward(dtype, trans_b):
         torch.cuda.synchronize()
         assert torch.equal(got, want)
     plan.close()
+
+
+def test_concurrent_host_threads_on_their_own_streams():
+    """Calls from four host threads at once, each on its own stream and dtype:
+    no host-side state is shared between calls, so every result equals the
+    single-threaded one (the reference's static host parameter buffer races
+    here, reference csrc/hopper_gmm_forward.cu:196)."""
+    import threading
+    g = torch.Generator().manual_seed(51)
+    cases = []
+    for i, dtype in enumerate([torch.bfloat16, torch.float16, torch.float32, torch.bfloat16]):
+        bs = torch.randint(0, 200, (6 + i,), generator=g)
+        bs[i] = 0
+        T = int(bs.sum())
+        a = torch.randn(T, 128, generator=g).to(dtype).cuda()
+        b = (torch.randn(len(bs), 128, 192, generator=g) / 12).to(dtype).cuda()
+        cases.append((a, b, bs, _fwd(a, b, bs, False)))
+    torch.cuda.synchronize()
+    errors = []
+
+    def work(i):
+        try:
+            torch.cuda.set_device(0)
+            s = torch.cuda.Stream()
+            a, b, bs, want = cases[i]
+            with torch.cuda.stream(s):
+                outs = [_fwd(a, b, bs, False) for _ in range(20)]
+            s.synchronize()
+            if not all(torch.equal(o, want) for o in outs):
+                errors.append(f"thread {i}: result differs")
+        except Exception as exc:  # noqa: BLE001
+            errors.append(f"thread {i}: {exc!r}")
+
+    threads = [threading.Thread(target=work, args=(i,)) for i in range(4)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    assert not errors, errors
