@@ -20,6 +20,7 @@ _SIGNATURES = {
     "gmm_sm100_errstr": (ctypes.c_char_p, [ctypes.c_int]),
     "gmm_sm100_last_error": (ctypes.c_char_p, []),
     "gmm_sm100_check_device": (ctypes.c_int, [ctypes.c_int]),
+    "gmm_sm100_set_tile_kind": (ctypes.c_int, [ctypes.c_int]),
     "gmm_sm100_workspace_size": (ctypes.c_size_t, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
                                                    ctypes.c_int64, ctypes.c_int64, ctypes.c_int,
                                                    ctypes.c_int]),
@@ -177,6 +178,18 @@ class Plan:
 
     def __del__(self):
         self.close()
+
+
+TILE_KINDS = {"auto": 0, "128": 1, "256": 2, "swap": 3}
+
+
+def set_tile_kind(kind: str) -> str:
+    """Force a kernel family for 16-bit problems ("auto", "128", "256" or "swap",
+    ``gmm_sm100_set_tile_kind``); returns the previous setting."""
+    prev = load().gmm_sm100_set_tile_kind(TILE_KINDS[kind])
+    if prev < 0:
+        _check(prev)
+    return {v: k for k, v in TILE_KINDS.items()}[prev]
 
 
 def device_error(clear=True) -> int:

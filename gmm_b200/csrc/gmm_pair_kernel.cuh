@@ -103,7 +103,7 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_pair_kernel(const __grid_cons
   if (p.dev_bs) {  // both CTAs of a pair build the same table
     int32_t* dtab = reinterpret_cast<int32_t*>(epi_stage + kEpiStageBytes);
     int32_t* meta = dtab + 3 * kMaxDevExperts + 2;
-    build_device_table(p, dtab, meta, reinterpret_cast<int*>(meta + 3));
+    build_device_table(p, dtab, meta, reinterpret_cast<long long*>(meta + 4));
     num_groups = meta[0];
     total_tiles = meta[1] * n_tiles;
     if (threadIdx.x == 0 && leader && meta[2] != 0) atomicCAS(&g_device_error, 0, meta[2]);

@@ -53,7 +53,11 @@ constexpr int kInlineGroups = 1024;  // groups whose table travels in the kernel
 constexpr int kInlineTableInts = 3 * kInlineGroups + 2;
 constexpr int kMaxPeers = 8;         // expert-parallel ranks a kernel can address
 constexpr int kMaxDevExperts = 1024;  // experts a device-built table can hold
-constexpr int kDevTableBytes = (3 * kMaxDevExperts + 64) * 4;  // row_off | tile_off | expert | meta | scan scratch
+constexpr int kDevTableBytes = (3 * kMaxDevExperts + 64) * 4;  // row_off | tile_off | expert | meta | 8-byte scan scratch
+// meta sits at int 3 * kMaxDevExperts + 2; the scan scratch (8 warps x 3
+// 64-bit values) at int 3 * kMaxDevExperts + 6, an 8-byte boundary.
+static_assert((3 * kMaxDevExperts + 6) % 2 == 0 && (3 * kMaxDevExperts + 6) * 4 + 24 * 8 <= kDevTableBytes,
+              "device table area");
 constexpr int kMBlock = 16;          // m-tiles per raster block (L2 reuse of B columns)
 constexpr int kThreads = 256;        // 8 warps: TMA, MMA, TMEM alloc, idle, 4x epilogue
 constexpr int kEpiStageBytes = 4 * 32 * 128;  // epilogue staging: 4 warps x 32 rows x 128 B
@@ -143,22 +147,23 @@ __device__ __forceinline__ TableView make_table_view(const GmmParams& p, const i
 }
 
 // Exclusive block scan (256 threads) of three per-thread values; returns the
-// block totals.  `scratch` holds 8 warps x 3 ints.
-__device__ __forceinline__ void block_scan3(int (&v)[3], int (&tot)[3], int* scratch) {
+// block totals.  64-bit, so that no sum of (possibly corrupt) device batch
+// sizes can wrap around.  `scratch` holds 8 warps x 3 values.
+__device__ __forceinline__ void block_scan3(long long (&v)[3], long long (&tot)[3], long long* scratch) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  int incl[3] = {v[0], v[1], v[2]};
+  long long incl[3] = {v[0], v[1], v[2]};
 #pragma unroll
   for (int d = 1; d < 32; d <<= 1) {
 #pragma unroll
     for (int j = 0; j < 3; ++j) {
-      const int o = __shfl_up_sync(0xffffffffu, incl[j], d);
+      const long long o = __shfl_up_sync(0xffffffffu, incl[j], d);
       if (lane >= d) incl[j] += o;
     }
   }
   if (lane == 31)
     for (int j = 0; j < 3; ++j) scratch[warp * 3 + j] = incl[j];
   __syncthreads();
-  int warp_off[3] = {0, 0, 0};
+  long long warp_off[3] = {0, 0, 0};
   for (int j = 0; j < 3; ++j) {
     tot[j] = 0;
     for (int w = 0; w < 8; ++w) {
@@ -172,13 +177,17 @@ __device__ __forceinline__ void block_scan3(int (&v)[3], int (&tot)[3], int* scr
 
 // Build the group table from device batch sizes into shared memory (all 256
 // threads).  Layout as the host table: row_off[G+1] | tile_off[G+1] |
-// expert[G]; meta[0] = G, meta[1] = m-tiles, meta[2] = error status.
-__device__ void build_device_table(const GmmParams& p, int32_t* tab, int32_t* meta, int* scratch) {
+// expert[G]; meta[0] = G, meta[1] = m-tiles, meta[2] = error status.  Row,
+// group and m-tile sums are taken in 64 bits: a negative size, or a total
+// above rows_cap (however large the sizes), leaves an empty table and an
+// error status, so no row past rows_cap is ever addressed.  After that check
+// every prefix fits in 32 bits (rows_cap < 2^31 - 256).
+__device__ void build_device_table(const GmmParams& p, int32_t* tab, int32_t* meta, long long* scratch) {
   const int E = p.dev_experts;
   const int BM = p.tile_rows;
   constexpr int kPer = kMaxDevExperts / kThreads;  // experts per thread (4)
   int bsv[kPer];
-  int loc[3] = {0, 0, 0};  // rows, non-empty experts, m-tiles of this thread's experts
+  long long loc[3] = {0, 0, 0};  // rows, non-empty experts, m-tiles of this thread's experts
   bool bad = false;
 #pragma unroll
   for (int i = 0; i < kPer; ++i) {
@@ -188,13 +197,13 @@ __device__ void build_device_table(const GmmParams& p, int32_t* tab, int32_t* me
     bsv[i] = m > 0 ? m : 0;
     loc[0] += bsv[i];
     loc[1] += bsv[i] > 0;
-    loc[2] += (bsv[i] + BM - 1) / BM;
+    loc[2] += (static_cast<long long>(bsv[i]) + BM - 1) / BM;
   }
-  int tot[3];
-  int pre[3] = {loc[0], loc[1], loc[2]};
+  long long tot[3];
+  long long pre[3] = {loc[0], loc[1], loc[2]};
   block_scan3(pre, tot, scratch);
   const int bad_any = __syncthreads_or(bad);
-  const int G = tot[1];
+  const int G = static_cast<int>(tot[1]);
   if (bad_any || tot[0] > p.rows_cap) {
     if (threadIdx.x == 0) {
       meta[0] = 0;
@@ -206,7 +215,7 @@ __device__ void build_device_table(const GmmParams& p, int32_t* tab, int32_t* me
     __syncthreads();
     return;
   }
-  int row = pre[0], g = pre[1], mt = pre[2];
+  int row = static_cast<int>(pre[0]), g = static_cast<int>(pre[1]), mt = static_cast<int>(pre[2]);
 #pragma unroll
   for (int i = 0; i < kPer; ++i) {
     if (bsv[i] > 0) {
@@ -219,10 +228,10 @@ __device__ void build_device_table(const GmmParams& p, int32_t* tab, int32_t* me
     row += bsv[i];
   }
   if (threadIdx.x == 0) {
-    tab[G] = tot[0];
-    tab[2 * G + 1] = tot[2];
+    tab[G] = static_cast<int>(tot[0]);
+    tab[2 * G + 1] = static_cast<int>(tot[2]);
     meta[0] = G;
-    meta[1] = tot[2];
+    meta[1] = static_cast<int>(tot[2]);
     meta[2] = 0;
   }
   __syncthreads();
@@ -482,7 +491,7 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_persistent_kernel(const __gri
   if (p.dev_bs) {
     int32_t* dtab = reinterpret_cast<int32_t*>(epi_stage + kEpiStageBytes);
     int32_t* meta = dtab + 3 * kMaxDevExperts + 2;
-    build_device_table(p, dtab, meta, reinterpret_cast<int*>(meta + 3));
+    build_device_table(p, dtab, meta, reinterpret_cast<long long*>(meta + 4));
     num_groups = meta[0];
     total_tiles = meta[1] * n_tiles;
     if (threadIdx.x == 0 && meta[2] != 0) atomicCAS(&g_device_error, 0, meta[2]);
@@ -988,17 +997,35 @@ int launch_swap(const GmmParams& prm, int grid, cudaStream_t stream, DeviceInfo*
 // when no expert has more than 64 rows (decode-shaped routing, where a
 // 128-row tile would be at least half padding) and neither the SwiGLU nor the
 // expert-parallel epilogue is needed; else single-CTA 128-row tiles.
-// GMM_SM100_TILE=128 / 256 / swap forces one of them (swap falls back to 128
-// for the SwiGLU and expert-parallel epilogues, which it does not have).
+// A process-wide override (gmm_sm100_set_tile_kind; initially from
+// GMM_SM100_TILE=128 / 256 / swap, read once) forces one of them (swap falls
+// back to 128 for the SwiGLU and expert-parallel epilogues, which it does not
+// have).
 enum TileKind { kTile128 = 0, kTilePair = 1, kTileSwap = 2 };
+
+std::atomic<int> g_tile_force{-1};  // a gmm_tile_kind; -1 = not initialised yet
+std::once_flag g_tile_force_once;
+
+int tile_force() {
+  std::call_once(g_tile_force_once, [] {
+    const char* s = std::getenv("GMM_SM100_TILE");
+    int k = GMM_TILE_AUTO;
+    if (s && std::strcmp(s, "128") == 0) k = GMM_TILE_128;
+    else if (s && std::strcmp(s, "256") == 0) k = GMM_TILE_PAIR;
+    else if (s && std::strcmp(s, "swap") == 0) k = GMM_TILE_SWAP;
+    int expect = -1;
+    g_tile_force.compare_exchange_strong(expect, k);  // a setter call that came first wins
+  });
+  return g_tile_force.load(std::memory_order_relaxed);
+}
 
 TileKind choose_tile_kind(const int64_t* bs, int64_t E, int64_t T, int dtype, int act, bool remote) {
   if (dtype == GMM_DTYPE_F32) return kTile128;
   const bool swap_ok = !act && !remote;
-  const char* force = std::getenv("GMM_SM100_TILE");
-  if (force && std::strcmp(force, "128") == 0) return kTile128;
-  if (force && std::strcmp(force, "256") == 0) return kTilePair;
-  if (force && std::strcmp(force, "swap") == 0) return swap_ok ? kTileSwap : kTile128;
+  const int force = tile_force();
+  if (force == GMM_TILE_128) return kTile128;
+  if (force == GMM_TILE_PAIR) return kTilePair;
+  if (force == GMM_TILE_SWAP) return swap_ok ? kTileSwap : kTile128;
   int64_t groups = 0, max_m = 0;
   for (int64_t e = 0; e < E; ++e) {
     groups += bs[e] > 0;
@@ -1295,6 +1322,14 @@ const char* gmm_sm100_errstr(int status) {
 
 const char* gmm_sm100_last_error(void) { return t_last_error.c_str(); }
 
+int gmm_sm100_set_tile_kind(int kind) {
+  if (kind < GMM_TILE_AUTO || kind > GMM_TILE_SWAP)
+    return fail(GMM_ERR_INVALID_ARGUMENT, "tile kind must be one of gmm_tile_kind");
+  const int prev = tile_force();
+  g_tile_force.store(kind, std::memory_order_relaxed);
+  return prev;
+}
+
 int gmm_sm100_check_device(int device) {
   DeviceInfo* di = nullptr;
   return device_info(device, &di);
@@ -1391,6 +1426,8 @@ int gmm_sm100_ep_gather(void* X, const void* const* src_peers, const int64_t* co
       const int64_t m = counts[e * world + j];
       if (m < 0 || src_rows[e * world + j] < 0) return fail(GMM_ERR_INVALID_ARGUMENT, "negative count or row");
       if (m == 0) continue;
+      if (src_rows[e * world + j] > INT32_MAX - m)  // the kernel indexes source rows in 32 bits
+        return fail(GMM_ERR_TOO_LARGE, "source rows beyond the 32-bit row range");
       if (n >= kMaxGatherChunks) return fail(GMM_ERR_TOO_LARGE, "too many (expert, rank) chunks");
       prm.chunk_dst[n] = static_cast<int>(rows);
       prm.chunk_rank[n] = (base + j) % world;
@@ -1480,10 +1517,10 @@ int gmm_sm100_forward_dev(const void* A, const void* B, const int32_t* batch_siz
   int64_t tile_rows = 128;
   bool swap = false;
   if (dtype != GMM_DTYPE_F32) {
-    const char* force = std::getenv("GMM_SM100_TILE");
-    if (force && std::strcmp(force, "256") == 0) tile_rows = 256;
-    else if (force && std::strcmp(force, "swap") == 0) swap = !swiglu;
-    else if (!(force && std::strcmp(force, "128") == 0)) {
+    const int force = tile_force();
+    if (force == GMM_TILE_PAIR) tile_rows = 256;
+    else if (force == GMM_TILE_SWAP) swap = !swiglu;
+    else if (force != GMM_TILE_128) {
       if (T >= 384 * E) tile_rows = 256;
       else swap = !swiglu && T <= 16 * E;
     }
@@ -1617,7 +1654,9 @@ namespace {
 std::mutex g_noalloc_mu;
 void* g_noalloc_addr[kMaxDevices] = {};
 
-// Device address of g_noalloc_scratch on device `dev` (which must be current).
+// Device address of g_noalloc_scratch on device `dev` (which must be current),
+// looked up once per device ordinal: the address in that device's primary
+// context, which is where the runtime API (and so every launch here) runs.
 int noalloc_scratch_address(int dev, void** out) {
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
   if (!g_noalloc_addr[dev]) {

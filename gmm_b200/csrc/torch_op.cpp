@@ -20,9 +20,12 @@
 #include <torch/library.h>
 
 #include "gmm_sm100.h"
+#include "hopper_gmm_forward.h"
 
-namespace gmm_b200 {
+namespace hpc_ops_hopper {
 
+// Declared in include/hopper_gmm_forward.h with the reference's signature
+// (reference csrc/hopper_gmm_forward.h:23-25).
 at::Tensor hopper_gmm_forward(at::Tensor A, at::Tensor B, at::Tensor batch_sizes, bool transb) {
   TORCH_CHECK(A.is_cuda() && A.is_contiguous(), "A must be a contiguous CUDA tensor");
   TORCH_CHECK(B.is_cuda() && B.is_contiguous(), "B must be a contiguous CUDA tensor");
@@ -70,6 +73,10 @@ at::Tensor hopper_gmm_forward(at::Tensor A, at::Tensor B, at::Tensor batch_sizes
   TORCH_CHECK(rc == GMM_OK, gmm_sm100_last_error());
   return D;
 }
+
+}  // namespace hpc_ops_hopper
+
+namespace gmm_b200 {
 
 // Fused MoE gate/up projection + SwiGLU: B holds [gate | up] (2*I output
 // columns); returns silu(A @ Bgate) * (A @ Bup), [T, I].  No reference
@@ -119,6 +126,6 @@ TORCH_LIBRARY(hopper_gmm_fwd, m) {
 }
 
 TORCH_LIBRARY_IMPL(hopper_gmm_fwd, CUDA, m) {
-  m.impl("gmm", &gmm_b200::hopper_gmm_forward);
+  m.impl("gmm", &hpc_ops_hopper::hopper_gmm_forward);
   m.impl("gmm_swiglu", &gmm_b200::gmm_swiglu);
 }

@@ -56,6 +56,18 @@ const char* gmm_sm100_errstr(int status);
 /* Detail of the last failure on the calling thread (thread-local storage). */
 const char* gmm_sm100_last_error(void);
 
+/* Kernel family override for 16-bit problems.  No reference counterpart (the
+ * reference has one CUTLASS configuration per dtype).  GMM_TILE_AUTO picks
+ * per problem (CTA-pair 256-row tiles when the non-empty experts average at
+ * least 384 rows, swap-AB tiles when no expert has more than 64 rows, else
+ * 128-row tiles); the others force one family (swap falls back to 128-row
+ * tiles for the SwiGLU and expert-parallel epilogues).  Process-wide; the
+ * initial value comes from the environment variable GMM_SM100_TILE
+ * (128 / 256 / swap), read once.  Takes effect for plans made afterwards.
+ * Returns the previous kind, or GMM_ERR_INVALID_ARGUMENT. */
+enum gmm_tile_kind { GMM_TILE_AUTO = 0, GMM_TILE_128 = 1, GMM_TILE_PAIR = 2, GMM_TILE_SWAP = 3 };
+int gmm_sm100_set_tile_kind(int kind);
+
 /* GMM_OK if `device` is a compute-capability 10.0 (B200-class) GPU.
  * Replaces the reference's compute-capability check
  * (reference csrc/hopper_gmm_forward.cu:389-397). */
@@ -90,8 +102,8 @@ int gmm_sm100_forward(const void* A, const void* B, const int64_t* batch_sizes,
  * down projections), from any thread and stream at once (it is never
  * modified after creation).  Replaces the reference's host-side problem
  * building, done again on every call (reference csrc/hopper_gmm_forward.cu:
- * 230-316 CutlassGroupedGemm, :454-471 segmentation).  The GMM_SM100_TILE
- * kernel override is read when the plan is made. */
+ * 230-316 CutlassGroupedGemm, :454-471 segmentation).  The kernel override
+ * (gmm_sm100_set_tile_kind) in force when the plan is made applies to it. */
 typedef struct gmm_sm100_plan_s gmm_sm100_plan_t;
 int gmm_sm100_plan(const int64_t* batch_sizes, int64_t num_experts, int64_t num_tokens, int64_t dim,
                    int64_t dim_out, int dtype, int trans_b, gmm_sm100_plan_t** plan_out);
@@ -238,7 +250,10 @@ size_t gmm_sm100_ep_workspace_size(const int64_t* counts, int64_t num_local_expe
  *
  * The first call on a device looks up the scratch array's device address
  * (cudaGetSymbolAddress) with that device current; make that first call
- * before any stream capture.  All calls share the one scratch array, and its
+ * before any stream capture.  The address is kept per device ordinal, so it
+ * belongs to the device's primary context, the one every CUDA runtime call
+ * works in; a caller that makes a different driver-API context current on
+ * the device (cuCtxSetCurrent) must not use this entry point.  All calls share the one scratch array, and its
  * contents are fully rewritten by each call before they are read: calls whose
  * GPU work overlaps (different streams, or different host threads, on one
  * device) race on it and must be serialised by the caller. */

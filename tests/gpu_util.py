@@ -2,6 +2,7 @@
 
 from __future__ import annotations
 
+import contextlib
 import json
 import os
 
@@ -60,3 +61,15 @@ def sampled_subproblem(bs, rows_per_expert=4, max_experts=8, seed=0):
         rows.extend(r)
         sub_bs.append(len(r))
     return np.asarray(rows, dtype=np.int64), pick, sub_bs
+
+
+@contextlib.contextmanager
+def forced_tile(kind):
+    """Force one kernel family ("auto", "128", "256", "swap") for the calls made
+    inside the block (``gmm_sm100_set_tile_kind``), then restore the previous one."""
+    from gmm_b200 import capi
+    prev = capi.set_tile_kind(kind)
+    try:
+        yield kind
+    finally:
+        capi.set_tile_kind(prev)

@@ -179,3 +179,17 @@ def test_plan_is_host_only_and_agrees_with_workspace_size():
     assert lib.gmm_sm100_launch(h, 16, 16, 16, None, 0, None) == 0
     lib.gmm_sm100_plan_free(h)
     lib.gmm_sm100_plan_free(None)
+
+
+def test_tile_kind_override_roundtrip():
+    """The process-wide kernel-family override (gmm_sm100_set_tile_kind)
+    returns the previous setting and rejects unknown kinds."""
+    from gmm_b200 import capi
+    prev = capi.set_tile_kind("128")
+    try:
+        assert capi.set_tile_kind("swap") == "128"
+        assert capi.set_tile_kind("256") == "swap"
+        assert capi.load().gmm_sm100_set_tile_kind(9) == -1
+        assert capi.set_tile_kind("auto") == "256"
+    finally:
+        capi.set_tile_kind(prev)

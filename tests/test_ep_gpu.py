@@ -29,7 +29,8 @@ def _worker(rank, world, port, E, dtype, trans_b, transport, tile):
     import sys
     sys.path.insert(0, ROOT)
     if tile != "auto":  # the single-GPU op and the EP layer must run the same kernel family
-        os.environ["GMM_SM100_TILE"] = tile
+        from gmm_b200 import capi
+        capi.set_tile_kind(tile)
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", init_method=f"file://{port}", rank=rank,

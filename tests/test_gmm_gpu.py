@@ -15,7 +15,7 @@ import torch
 
 import oracle
 from cases import make_case_inputs
-from gpu_util import check_rows, golden, golden_values, sampled_subproblem
+from gpu_util import check_rows, forced_tile, golden, golden_values, sampled_subproblem
 
 pytestmark = pytest.mark.gpu
 
@@ -34,12 +34,12 @@ def _device():
 
 
 @pytest.fixture(params=["128", "256", "swap"])
-def tile(request, monkeypatch):
+def tile(request):
     """Run a test with one kernel forced: single-CTA 128-row tiles, CTA-pair
     256-row tiles, or swap-AB tiles (16-bit problems only; fp32 keeps its own
     kernel)."""
-    monkeypatch.setenv("GMM_SM100_TILE", request.param)
-    return request.param
+    with forced_tile(request.param):
+        yield request.param
 
 
 def _fwd(a, b, bs, trans_b):
@@ -236,10 +236,9 @@ def test_host_streamed_matches_device_op(dtype, trans_b):
         assert torch.equal(got, want)
 
 
-def test_default_swap_tiles_match_the_128_row_kernel_and_the_oracle(monkeypatch):
+def test_default_swap_tiles_match_the_128_row_kernel_and_the_oracle():
     """Decode-shaped routing (small experts) takes swap-AB tiles by default;
     their output must agree with the 128-row kernel and the oracle."""
-    monkeypatch.delenv("GMM_SM100_TILE", raising=False)
     g = torch.Generator().manual_seed(21)
     bs = torch.randint(0, 17, (96,), generator=g)
     bs[::5] = 0
@@ -249,10 +248,10 @@ def test_default_swap_tiles_match_the_128_row_kernel_and_the_oracle(monkeypatch)
         a = torch.randn(T, dim, generator=g).to(dtype)
         shape = (len(bs), dim_out, dim) if trans_b else (len(bs), dim, dim_out)
         b = (torch.randn(*shape, generator=g) / dim ** 0.5).to(dtype)
-        auto = _fwd(a.cuda(), b.cuda(), bs, trans_b).cpu()
-        monkeypatch.setenv("GMM_SM100_TILE", "128")
-        big = _fwd(a.cuda(), b.cuda(), bs, trans_b).cpu()
-        monkeypatch.delenv("GMM_SM100_TILE")
+        with forced_tile("auto"):
+            auto = _fwd(a.cuda(), b.cuda(), bs, trans_b).cpu()
+        with forced_tile("128"):
+            big = _fwd(a.cuda(), b.cuda(), bs, trans_b).cpu()
         name = oracle.dtype_name(dtype)
         want = oracle.round_to(oracle.gmm_oracle_c(a, b, bs, trans_b), name)
         for got in (auto, big):

@@ -10,7 +10,7 @@ import pytest
 import torch
 
 import oracle
-from gpu_util import sampled_subproblem
+from gpu_util import forced_tile, sampled_subproblem
 
 pytestmark = pytest.mark.gpu
 
@@ -23,9 +23,9 @@ def _device():
 
 
 @pytest.fixture(params=["128", "256", "swap"])
-def tile(request, monkeypatch):
-    monkeypatch.setenv("GMM_SM100_TILE", request.param)
-    return request.param
+def tile(request):
+    with forced_tile(request.param):
+        yield request.param
 
 
 def _inputs(bs, dim, inter, dtype, trans_b, seed=0):

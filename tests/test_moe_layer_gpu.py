@@ -10,6 +10,7 @@ import pytest
 import torch
 
 import oracle
+from gpu_util import forced_tile
 
 pytestmark = pytest.mark.gpu
 
@@ -25,9 +26,9 @@ def _device():
 
 
 @pytest.fixture(params=["128", "256", "swap"])
-def tile(request, monkeypatch):
-    monkeypatch.setenv("GMM_SM100_TILE", request.param)
-    return request.param
+def tile(request):
+    with forced_tile(request.param):
+        yield request.param
 
 
 @pytest.mark.parametrize("E,k,dtype", [(8, 2, torch.float32), (128, 8, torch.bfloat16),
