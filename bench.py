@@ -6,18 +6,27 @@ One JSON line on rank 0.  A "step" is one grouped-GEMM forward over the
 configuration's full synthetic batch.
 
 * N = 1 (default workload cfg2, the configuration the headline metric is
-  quoted on): ``value`` = FLOPs / step time of ``hopper_gmm_fwd`` with inputs
-  resident in HBM (all inputs are larger than the 126 MB L2, so no flush is
-  needed); ``e2e`` = the same metric through the same public call with the
-  inputs copied in from pinned host memory and D copied back every step.
+  quoted on): ``value`` = FLOPs / mean step time of ``hopper_gmm_fwd`` with
+  inputs resident in HBM (CUDA events per step; the inputs are larger than
+  the 126 MB L2); ``e2e`` = the same metric through the public host-operand
+  call with A, B copied in from pinned host memory and D copied back every
+  step; ``parity`` = sampled output rows of every expert against a PyTorch
+  fp32 reference on the GPU; ``roofline.sustained_loop`` = >= 1 s of
+  back-to-back steps after the timed region with the SM clock seen under
+  load and the fraction of the dense tensor rate at that clock;
+  ``configs`` = kernel time, roofline and parity of the other four
+  workloads (cfg4's ``p50_us_per_call`` is its headline); ``ep_configs`` =
+  the expert-parallel workloads (cfg5, cfg3) at N = 1, i.e. the local GEMM.
 * N > 1 (launched by torchrun): expert parallelism -- each rank owns
-  E/N experts and a 1/N share of the tokens; a step is dispatch all-to-all +
-  local grouped GEMM + combine all-to-all (``gmm_b200.ep``).  ``value`` =
-  whole-job FLOPs / max-over-ranks step time; ``tokens_per_s`` = pre-top-k
-  tokens / step time.
+  E/N experts and a 1/N share of the tokens (``gmm_b200.ep_bench``): the
+  headline is cfg2 weak-scaled, ``ep_configs`` holds cfg5 and cfg3
+  strong-scaled with in-run parity on every rank.  ``value`` = whole-job
+  FLOPs / max-over-ranks step time; ``tokens_per_s`` = pre-top-k tokens /
+  step time.
 * ``--impl reference``: the reference's own CPU path (its per-expert
   ``ref_gmm`` loop, restated in ``oracle.ref_gmm_port``) on the host cores,
-  on a bounded row sample of the same workload; rank 0 only.
+  on a bounded row sample of the same workload; rank 0 only; loads none of
+  this repository's CUDA libraries.
 """
 
 from __future__ import annotations
@@ -58,6 +67,13 @@ def parse():
     ap.add_argument("--layer", action="store_true",
                     help="time the device-resident MoE layer (routing, permute, SwiGLU FFN, combine) "
                          "eagerly and as a replayed CUDA graph")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the per-configuration lines (configs / ep_configs)")
+    ap.add_argument("--sustain-s", type=float, default=1.0,
+                    help="seconds of back-to-back steps after the timed region, for the clock record")
+    ap.add_argument("--phases", action="store_true",
+                    help="N > 1: also time each phase of one expert-parallel step (barriers, gather, "
+                         "GEMM + combine), max over ranks")
     ap.add_argument("--kernel-only", action="store_true",
                     help="warm-up + timed launches only (no e2e / CPU baseline / clocks): the "
                          "command profiled with ncu")
@@ -83,15 +99,22 @@ def load_traffic(key):
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle sampling around the timed region."""
+    """nvidia-smi clock / throttle sampling around the timed region.
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    ``mark()`` notes host times; ``summary(window=i)`` restricts to the samples
+    taken between mark i-1 and mark i (window 0: the whole span).  ``sm_mhz``
+    is the median over the samples drawn under load (power above 40% of the
+    largest sample), so idle samples around a short timed region do not count."""
+
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, index):
         self.index = index
         self.proc = None
+        self.marks = []
+        self.lines = []
 
     def __enter__(self):
         if self.index < 0:
@@ -106,8 +129,10 @@ class ClockSampler:
         time.sleep(0.15)
         return self
 
+    def mark(self):
+        self.marks.append(time.time())
+
     def __exit__(self, *exc):
-        self.lines = []
         if self.proc is not None:
             time.sleep(0.1)
             self.proc.terminate()
@@ -118,25 +143,35 @@ class ClockSampler:
                 out, _ = self.proc.communicate()
             self.lines = [ln for ln in out.splitlines() if ln.strip()]
 
-    def summary(self):
-        sm, mx, reasons = [], None, set()
+    def _samples(self):
+        import datetime
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in getattr(self, "lines", []):
+        for ln in self.lines:
             parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10:
                 continue
             try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
+                ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                sm, mx = float(parts[2]), float(parts[3])
+                pw = float(parts[4]) if parts[4] not in ("", "[N/A]") else 0.0
             except ValueError:
                 continue
-            for n, v in zip(names, parts[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(n)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+            act = [n for n, v in zip(names, parts[6:10]) if v.lower().startswith("active")]
+            yield ts, sm, mx, pw, act
+
+    def summary(self, window=0):
+        samples = list(self._samples())
+        if window and len(self.marks) > window:
+            lo, hi = self.marks[window - 1], self.marks[window]
+            samples = [x for x in samples if lo <= x[0] <= hi]
+        if not samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        pmax = max(x[3] for x in samples)
+        loaded = [x for x in samples if x[3] >= 0.4 * pmax] or samples
+        reasons = sorted({r for x in loaded for r in x[4]})
+        return {"sm_mhz": statistics.median(x[1] for x in loaded), "sm_max_mhz": samples[-1][2],
+                "reasons": reasons, "samples": len(samples), "samples_under_load": len(loaded),
+                "power_w_max": pmax}
 
 
 def cpu_rate(cfg, a_cpu, b_cpu, bs, budget_s=10.0):
@@ -182,65 +217,148 @@ def cpu_rate(cfg, a_cpu, b_cpu, bs, budget_s=10.0):
     return flops / med / 1e12, desc, cores
 
 
-def cpu_inputs(cfg, a_dev, b_dev, bs, max_rows_per_expert=None):
-    """CPU copies of the device inputs (the exact bytes the kernel saw)."""
-    return a_dev.cpu(), b_dev.cpu()
-
-
 # ------------------------------------------------------------------------ N = 1
+def _workloads():
+    """``gmm_b200/configs.py`` (seeded workload generators, no CUDA code) loaded by
+    file path: importing it as ``gmm_b200.configs`` would run the package's
+    ``__init__``, which loads the CUDA libraries -- the reference arm must not."""
+    import importlib.util
+    name = "gmm_b200_workloads"
+    if name not in sys.modules:
+        spec = importlib.util.spec_from_file_location(name, os.path.join(ROOT, "gmm_b200", "configs.py"))
+        mod = importlib.util.module_from_spec(spec)
+        sys.modules[name] = mod
+        spec.loader.exec_module(mod)
+    return sys.modules[name]
+
+
+def _events_time(fn, steps, flush=None):
+    """Per-step device milliseconds of ``fn`` (CUDA events on the current stream)."""
+    import torch
+    stream = torch.cuda.current_stream()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    torch.cuda.synchronize()
+    for i in range(steps):
+        if flush is not None:
+            flush.zero_()
+        starts[i].record(stream)
+        fn()
+        ends[i].record(stream)
+    torch.cuda.synchronize()
+    return [s_.elapsed_time(e) for s_, e in zip(starts, ends)]
+
+
+DENSE_FLOP_PER_CLK = 148 * 8192  # B200: 148 SMs x 4096 bf16/fp16 FMA per clock each (dense)
+
+
+def _config_inputs(W, cid, dev):
+    import torch
+    cfg = W.CONFIGS[cid]
+    bs = W.batch_sizes_for(cfg)
+    if cid == 1:
+        a, b = [t.to(dev) for t in W.make_inputs(cfg, "cpu")]
+    else:
+        a, b = W.make_inputs(cfg, "cuda")
+    torch.cuda.synchronize()
+    return cfg, bs, a, b
+
+
+def _config_entry(W, cid, dev, steps, warmup, peaks):
+    """Kernel time, roofline and parity of one workload at N = 1."""
+    import torch
+    from gmm_b200 import hopper_gmm_fwd
+    from gmm_b200.ep_bench import check_parity
+    cfg, bs, a, b = _config_inputs(W, cid, dev)
+    fn = lambda: hopper_gmm_fwd(a, b, bs, cfg.trans_b)  # noqa: E731
+    for _ in range(max(3, warmup)):
+        fn()
+    alg = cfg.algorithmic_bytes(bs)
+    flush = torch.empty(int(256e6), dtype=torch.uint8, device=dev) if alg <= 2 * 126e6 else None
+    ms = _events_time(fn, steps, flush)
+    mean = statistics.fmean(ms)
+    out = fn()
+    par = check_parity(out, a, bs.tolist(), lambda e: b[e], cfg.trans_b)
+    tflops = cfg.flops() / (mean * 1e-3) / 1e12
+    gbs = alg / (mean * 1e-3) / 1e9
+    hbm_bound = cfg.dtype == torch.float32 or cid in (3, 4)
+    entry = {"workload": f"cfg{cid}: {cfg.name}",
+             "dtype": {torch.bfloat16: "bf16", torch.float16: "fp16", torch.float32: "fp32"}[cfg.dtype],
+             "ms_per_step": round(mean, 5), "p50_us_per_call": round(statistics.median(ms) * 1e3, 2),
+             "tflops": round(tflops, 2), "gbs": round(gbs, 1),
+             "tokens_per_s": round(cfg.tokens / (mean * 1e-3), 1),
+             "roofline": {"bound": "hbm" if hbm_bound else "tensor",
+                          "frac": round(gbs / peaks["hbm_gbs"] if hbm_bound else tflops / peaks["bf16_tflops"], 4),
+                          "peak": peaks["hbm_gbs"] if hbm_bound else peaks["bf16_tflops"],
+                          "unit": "GB/s" if hbm_bound else "TFLOP/s"},
+             "l2": W.l2_note(cfg, bs), "steps": steps, "parity": par,
+             "kernel_launches_per_step": 2 if cfg.dtype == torch.float32 else 1}
+    del a, b, out, flush
+    torch.cuda.empty_cache()
+    return entry
+
+
 def run_single(args):
     import torch
-    import gmm_b200
+    import gmm_b200  # noqa: F401  (loads the operator; fails loudly without it)
     from gmm_b200 import hopper_gmm_fwd
-    from gmm_b200.configs import CONFIGS, batch_sizes_for, make_inputs
+    from gmm_b200.ep_bench import check_parity
+    W = _workloads()
 
     cid = args.config or 2
-    cfg = CONFIGS[cid]
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    bs = batch_sizes_for(cfg)
+    cfg = W.CONFIGS[cid]
+    bs = W.batch_sizes_for(cfg)
     if args.max_experts:
         import dataclasses
         bs = bs[:args.max_experts].clone()
         cfg = dataclasses.replace(cfg, num_experts=len(bs), tokens=int(bs.sum()), top_k=1)
     if cid == 1:
-        a, b = [t.to(dev) for t in make_inputs(cfg, "cpu")]
+        a, b = [t.to(dev) for t in W.make_inputs(cfg, "cpu")]
     else:
-        a, b = make_inputs(cfg, "cuda")
+        a, b = W.make_inputs(cfg, "cuda")
     flops = cfg.flops()
     alg_bytes = cfg.algorithmic_bytes(bs)
     launches_per_step = 2 if cfg.dtype == torch.float32 else 1  # fp32: split pre-pass + GEMM
 
-    stream = torch.cuda.current_stream()
+    def step():
+        return hopper_gmm_fwd(a, b, bs, cfg.trans_b)
+
     for _ in range(max(3, args.warmup)):
-        hopper_gmm_fwd(a, b, bs, cfg.trans_b)
+        step()
     torch.cuda.synchronize()
-    l2_note = "inputs larger than L2 (126 MB)" if alg_bytes > 2 * 126e6 else "L2 flushed between steps"
     flush = torch.empty(int(256e6), dtype=torch.uint8, device=dev) if alg_bytes <= 2 * 126e6 else None
 
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    peaks, peak_src = load_peaks()
     with ClockSampler(-1 if args.kernel_only else 0) as clk:
-        torch.cuda.synchronize()
-        t0 = torch.cuda.Event(enable_timing=True)
-        t1 = torch.cuda.Event(enable_timing=True)
-        t0.record(stream)
-        for i in range(args.steps):
-            if flush is not None:
-                flush.zero_()
-            starts[i].record(stream)
-            hopper_gmm_fwd(a, b, bs, cfg.trans_b)
-            ends[i].record(stream)
-        t1.record(stream)
-        torch.cuda.synchronize()
-    kernel_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+        kernel_ms = _events_time(step, args.steps, flush)
+        # Sustained: back to back for >= args.sustain_s seconds right after the
+        # timed region, so the clock sampler sees the kernel under load.
+        sus = None
+        if not args.kernel_only and args.sustain_s > 0:
+            n = max(1, int(args.sustain_s * 1e3 / max(statistics.fmean(kernel_ms), 1e-3)))
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            clk.mark()
+            e0.record()
+            for _ in range(n):
+                if flush is not None:
+                    flush.zero_()
+                step()
+            e1.record()
+            torch.cuda.synchronize()
+            clk.mark()
+            sus = (n, e0.elapsed_time(e1) / n)
     step_ms = statistics.fmean(kernel_ms)
+    value = flops / (step_ms * 1e-3) / 1e12
     if args.kernel_only:
-        print(json.dumps({"config": f"cfg{cid}", "ms_per_step": step_ms,
-                          "value": flops / (step_ms * 1e-3) / 1e12, "unit": "TFLOP/s"}), flush=True)
+        print(json.dumps({"config": f"cfg{cid}", "ms_per_step": step_ms, "value": value,
+                          "unit": "TFLOP/s"}), flush=True)
         return
     p50_us = statistics.median(kernel_ms) * 1e3
-    value = flops / (step_ms * 1e-3) / 1e12
+    out = step()
+    parity = check_parity(out, a, bs.tolist(), lambda e: b[e], cfg.trans_b)
+    del out
 
     # ---------------- e2e: pinned host buffers, copies inside the timed region
     from gmm_b200 import hopper_gmm_fwd_host
@@ -257,77 +375,112 @@ def run_single(args):
     torch.cuda.synchronize()
     e_steps = max(1, min(args.e2e_steps, args.steps))
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
+    e0.record()
     for _ in range(e_steps):
         e2e_step()
-    e1.record(stream)
+    e1.record()
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / e_steps
     es = a.element_size()
     h2d = (a.numel() + b.numel()) * es
     d2h = cfg.rows * cfg.dim_out * es
 
-    peaks, peak_src = load_peaks()
     if cfg.dtype == torch.float32 or cid in (3, 4):
         bound, achieved, peak, unit = "hbm", alg_bytes / (step_ms * 1e-3) / 1e9, peaks["hbm_gbs"], "GB/s"
     else:
         bound, achieved, peak, unit = "tensor", value, peaks["bf16_tflops"], "TFLOP/s"
     traffic = load_traffic(f"cfg{cid}")
+    clocks = clk.summary()
+    roof = {"bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": unit,
+            "frac": round(achieved / peak, 4), "traffic": traffic,
+            "peak_source": f"{peak_src} ({'burst' if unit == 'TFLOP/s' else 'copy'})",
+            "algorithmic": {"flops": flops, "bytes": alg_bytes}}
+    if unit == "TFLOP/s" and peaks.get("bf16_tflops_sustained"):
+        roof["peak_sustained"] = peaks["bf16_tflops_sustained"]
+        roof["frac_sustained"] = round(achieved / peaks["bf16_tflops_sustained"], 4)
+    if sus is not None:
+        n, sms = sus
+        s_val = flops / (sms * 1e-3) / 1e12
+        s_mhz = clk.summary(window=1).get("sm_mhz")
+        roof["sustained_loop"] = {
+            "steps": n, "ms_per_step": round(sms, 4), "achieved": round(s_val if unit == "TFLOP/s"
+                                                                       else alg_bytes / (sms * 1e-3) / 1e9, 2),
+            "sm_mhz_median": s_mhz, "power_w_max": clk.summary(window=1).get("power_w_max")}
+        if s_mhz and unit == "TFLOP/s":
+            per_ghz = s_val / (s_mhz / 1e3)
+            roof["sustained_loop"]["tflops_per_ghz"] = round(per_ghz, 2)
+            roof["sustained_loop"]["frac_at_clock"] = round(per_ghz / (DENSE_FLOP_PER_CLK / 1e3), 4)
+            roof["sustained_loop"]["note"] = ("frac_at_clock = achieved / (148 SMs x 8192 dense FLOP/clk "
+                                              "x median SM clock under load)")
 
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 4),
         "p50_us_per_call": round(p50_us, 2),
         "tokens_per_s": round(cfg.tokens / (step_ms * 1e-3), 1),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "higher_is_better": True, "scaling": "weak" if cid == 2 else "strong", "vs_baseline": None,
         "dtype": {torch.bfloat16: "bf16", torch.float16: "fp16", torch.float32: "fp32"}[cfg.dtype],
         "data": "synthetic (seeded routing -> batch_sizes; A ~ N(0,1), B ~ N(0,1/dim))",
-        "config": {"workload": f"cfg{cid}: {cfg.name}", "experts": cfg.num_experts,
-                   "dim": cfg.dim, "dim_out": cfg.dim_out, "tokens": cfg.tokens,
-                   "top_k": cfg.top_k, "rows": cfg.rows, "trans_b": cfg.trans_b,
-                   "parallelism": "ep1", "l2": l2_note},
+        "config": W.workload_config(cfg, 1, weak=cid == 2),
+        "parity": parity,
         "e2e": {"value": round(flops / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
                 "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h),
                 "path": "gmm_b200.hopper_gmm_fwd_host: pinned host A,B -> device, GEMM, "
                         "D -> pinned host, pipelined per expert chunk on 3 streams"},
         "gpu_launches": args.steps * launches_per_step,
-        "roofline": {"bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": unit,
-                     "frac": round(achieved / peak, 4), "traffic": traffic,
-                     "peak_source": f"{peak_src} ({'burst' if unit == 'TFLOP/s' else 'copy'})",
-                     **({"peak_sustained": peaks.get("bf16_tflops_sustained"),
-                         "frac_sustained": round(achieved / peaks["bf16_tflops_sustained"], 4)}
-                        if unit == "TFLOP/s" and peaks.get("bf16_tflops_sustained") else {}),
-                     "algorithmic": {"flops": flops, "bytes": alg_bytes}},
-        "clocks": clk.summary(),
+        "roofline": roof,
+        "clocks": clocks,
     }
     if not args.no_cpu_baseline:
-        a_c, b_c = cpu_inputs(cfg, a, b, bs)
+        a_c, b_c = a.cpu(), b.cpu()
         rate, desc, cores = cpu_rate(cfg, a_c, b_c, bs)
         line["cpu_baseline"] = {"value": round(rate, 4), "unit": "TFLOP/s", "cores": cores,
                                 "kind": "port", "sample": desc}
+        del a_c, b_c
+    del a, b, a_h, b_h, d_h
+    torch.cuda.empty_cache()
+    if not args.no_configs and not args.max_experts:
+        configs = {}
+        for ocid in (1, 2, 3, 4, 5):
+            if ocid != cid:
+                configs[f"cfg{ocid}"] = _config_entry(W, ocid, dev, max(5, min(args.steps, 20)),
+                                                      args.warmup, peaks)
+        line["configs"] = configs
+        # expert parallelism at N = 1 is the local grouped GEMM
+        line["ep_configs"] = {
+            k: {"workload": v["workload"], "dtype": v["dtype"], "scaling": "strong",
+                "tokens": W.CONFIGS[int(k[3:])].tokens,
+                "experts_per_rank": W.CONFIGS[int(k[3:])].num_experts,
+                "ms_per_step": v["ms_per_step"], "tokens_per_s": v["tokens_per_s"],
+                "tflops": v["tflops"], "n_gpus": 1, "parity": v["parity"],
+                "load_imbalance": {"efficiency_ceiling": 1.0}}
+            for k, v in configs.items() if k in ("cfg5", "cfg3")}
     print(json.dumps(line), flush=True)
 
 
 # ------------------------------------------------------------------ reference arm
 def run_reference(args):
+    """The reference's own CPU path on the host cores.  Imports torch, the
+    workload generators (by file path) and ``oracle`` -- nothing that loads
+    this repository's CUDA libraries."""
     import torch
-    from gmm_b200.configs import CONFIGS, batch_sizes_for, make_inputs
     import oracle
+    W = _workloads()
 
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
     cid = args.config or 2
-    cfg = CONFIGS[cid]
-    bs = batch_sizes_for(cfg)
+    cfg = W.CONFIGS[cid]
+    bs = W.batch_sizes_for(cfg)
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
     # Bounded sample: every expert's full B, the first r rows of each expert,
     # r sized so one step takes about a second on this host.
     gen = torch.Generator().manual_seed(cfg.seed)
-    from gmm_b200.configs import b_shape
-    shape = b_shape(cfg)
+    shape = W.b_shape(cfg)
     b = torch.empty(*shape, dtype=cfg.dtype)
     for e in range(shape[0]):
         b[e] = (torch.randn(*shape[1:], generator=gen) / math.sqrt(cfg.dim)).to(cfg.dtype)
@@ -358,15 +511,14 @@ def run_reference(args):
     desc = (f"reference ref_gmm restated (oracle.ref_gmm_port, torch CPU "
             f"{oracle.dtype_name(cfg.dtype)}) on the first {min(r, max(bsl))} rows of each expert "
             f"({rows} of {cfg.rows} rows, full B); {len(times)} timed steps")
+    weak = cid == 2
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "TFLOP/s",
         "n_gpus": args.gpus, "steps": len(times), "warmup": args.warmup,
-        "ms_per_step": round(step * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": round(step * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak" if weak else "strong",
         "vs_baseline": None, "dtype": oracle.dtype_name(cfg.dtype), "data": "synthetic",
-        "config": {"workload": f"cfg{cid}: {cfg.name}", "experts": cfg.num_experts, "dim": cfg.dim,
-                   "dim_out": cfg.dim_out, "tokens": cfg.tokens, "top_k": cfg.top_k,
-                   "rows": cfg.rows, "trans_b": cfg.trans_b, "parallelism": "cpu host",
-                   "sampled_rows": rows},
+        "config": W.workload_config(cfg, world, weak),
         "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": cores,
                          "kind": "port", "sample": desc},
         "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,

@@ -62,6 +62,13 @@ _SIGNATURES = {
     "gmm_sm100_ep_gather": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                            ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_int,
                                            ctypes.c_int64, ctypes.c_void_p]),
+    "gmm_sm100_forward_inject_timeout": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                                        ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                                        ctypes.c_int64, ctypes.c_int, ctypes.c_int,
+                                                        ctypes.c_void_p, ctypes.c_int, ctypes.c_double,
+                                                        ctypes.c_void_p]),
+    "gmm_sm100_ep_barrier": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                            ctypes.c_double, ctypes.c_void_p]),
     "gmm_sm100_forward_ep": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                             ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_int,
                                             ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
@@ -214,6 +221,13 @@ def ep_gather(x, src_ptrs, counts, src_rows, num_local_experts, row_bytes, rank_
     s = torch.cuda.current_stream(x.device).cuda_stream if stream is None else stream
     _check(load().gmm_sm100_ep_gather(x.data_ptr(), _ptrs(src_ptrs), c.ctypes.data, r.ctypes.data,
                                       num_local_experts, len(src_ptrs), rank_base, row_bytes, s))
+
+
+def ep_barrier(flag_ptrs, rank, epoch, device, timeout_s=5.0, stream=None):
+    """Cross-rank barrier over peer memory (``gmm_sm100_ep_barrier``)."""
+    import torch
+    s = torch.cuda.current_stream(device).cuda_stream if stream is None else stream
+    _check(load().gmm_sm100_ep_barrier(_ptrs(flag_ptrs), len(flag_ptrs), rank, epoch, timeout_s, s))
 
 
 def forward_ep(x, b, counts, dst_rows, num_local_experts, out_ptrs, trans_b=False, rank_base=0,

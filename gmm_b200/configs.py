@@ -146,3 +146,23 @@ def make_inputs(cfg: GmmConfig, device: str = "cpu", rows: Optional[int] = None,
             t = torch.randn(*shape[1:], generator=gen, device=dev, dtype=torch.float32)
             b[e].copy_(t.mul_(s))
     return a, b
+
+
+TOLERANCE = {torch.bfloat16: 1.6e-2, torch.float16: 2e-3, torch.float32: 5e-3}  # rtol = atol
+
+
+def l2_note(cfg: GmmConfig, batch_sizes) -> str:
+    """How a timed loop over this workload avoids L2 reuse between steps."""
+    return ("inputs larger than L2 (126 MB)" if cfg.algorithmic_bytes(batch_sizes) > 2 * 126e6
+            else "L2 flushed between steps (256 MB write)")
+
+
+def workload_config(cfg: GmmConfig, world: int = 1, weak: bool = False) -> dict:
+    """The ``config`` object of a bench line: the workload alone, identical in
+    every arm that measures it (no arm- or implementation-specific keys)."""
+    tokens = cfg.tokens * world if weak else cfg.tokens
+    return {"workload": f"cfg{cfg.cid}: {cfg.name}", "experts": cfg.num_experts, "dim": cfg.dim,
+            "dim_out": cfg.dim_out, "tokens": tokens, "top_k": cfg.top_k,
+            "rows": tokens * cfg.top_k, "trans_b": cfg.trans_b, "parallelism": f"ep{world}",
+            "scaling": "weak" if weak else "strong",
+            "l2": l2_note(cfg, batch_sizes_for(cfg))}

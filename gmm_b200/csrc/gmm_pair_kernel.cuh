@@ -16,6 +16,17 @@
 //     leader's accumulator-empty barrier (count 8) through the cluster window.
 // Per CTA this moves 32 KB of operands per 64-deep k-block for the same MMA
 // work the single-CTA 128x256 tile needs 48 KB for.
+//
+// Half tiles: the last m-tile of an expert whose remaining rows fit in 128
+// runs as a 128 x 256 pair MMA (M = 128, cta_group::2): each CTA loads 64 A
+// rows (a 64-row TMA box, tmap_a2) and its usual 128 B columns, and half the
+// tensor work of a 256-row tile is spent on padding rows no more.  The
+// accumulator of such an MMA sits in TMEM as the "2x2" data-path layout: in
+// each CTA, row m (0..63) of output columns [0, 128) is TMEM lane m and of
+// columns [128, 256) lane 64 + m, both at accumulator columns [0, 128) -- so
+// epilogue warp q drains rows 32 (q & 1) .. +31 of column half q >> 1.  The
+// SwiGLU epilogue pairs gate and up columns inside one thread's row, which
+// this layout splits across lanes, so SwiGLU launches keep 256-row tiles.
 #pragma once
 
 template <int kKind, bool kBMnMajor>
@@ -35,6 +46,8 @@ struct PairCfg {
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = 2 * BN;
   static constexpr uint32_t kIdesc = make_idesc(kKind == kKindBf16 ? 1u : 0u, kBMnMajor, BM, BN);
+  static constexpr uint32_t kIdescHalf = make_idesc(kKind == kKindBf16 ? 1u : 0u, kBMnMajor, BM / 2, BN);
+  static constexpr int kHalfABytes = kABytes / 2;  // 64 A rows per CTA in a half tile
   static constexpr int kBarBytes = 256;
   static constexpr int kSmemBytes = kStages * kStageBytes + kBarBytes + kEpiStageBytes + kDevTableBytes + 1024;
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
@@ -83,6 +96,7 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_pair_kernel(const __grid_cons
   }
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&p.tmap_a);
+    prefetch_tmap(&p.tmap_a2);
     prefetch_tmap(&p.tmap_b);
   }
   if (warp == 2) {
@@ -98,6 +112,8 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_pair_kernel(const __grid_cons
 
   const int n_tiles = p.n_tiles;
   const int k_blocks = p.k_blocks;
+  const unsigned long long wait_ns = p.wait_ns ? p.wait_ns : kWaitTimeoutNs;
+  const bool halves = !p.act;  // half tiles for expert tails of <= 128 rows
   int num_groups = p.num_groups, total_tiles = p.total_tiles;
   const int32_t* tab = p.ext_table ? p.ext_table : p.inline_table;
   if (p.dev_bs) {  // both CTAs of a pair build the same table
@@ -123,22 +139,30 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_pair_kernel(const __grid_cons
       int g = 0;
       for (int tile = pair; ok && tile < total_tiles; tile += num_pairs) {
         const Tile t = decode_tile<C::BM, C::BN>(tv, n_tiles, tile, g);
-        const int arow = t.row0 + C::BM_CTA * static_cast<int>(cta);
+        const bool half = halves && t.rows <= C::BM_CTA;
+        const int arow = t.row0 + (half ? C::BM_CTA / 2 : C::BM_CTA) * static_cast<int>(cta);
         // SwiGLU: the leader holds the tile's 128 gate columns, the peer the matching up columns.
         const int bcol = !p.act ? t.n0 + C::BN_CTA * static_cast<int>(cta)
                                 : (t.n0 >> 1) + (cta ? p.act_cols : 0);
         for (int kb = 0; kb < k_blocks; ++kb) {
-          if (!mbar_wait(smem_u32(empty_bar + stage), phase ^ 1, abort_flag)) {
+          if (!mbar_wait(smem_u32(empty_bar + stage), phase ^ 1, abort_flag, wait_ns)) {
             ok = false;
             break;
           }
+          if (kb + 1 == p.drop_kb1 && tile == 0) {  // timeout test hook: this stage never fills
+            if (++stage == C::kStages) {
+              stage = 0;
+              phase ^= 1;
+            }
+            continue;
+          }
           const uint32_t fb_local = smem_u32(full_bar + stage);
-          if (leader) mbar_arrive_expect_tx(fb_local, 2 * C::kStageBytes);
+          if (leader) mbar_arrive_expect_tx(fb_local, 2 * (half ? C::kHalfABytes + C::kBBytes : C::kStageBytes));
           const uint32_t fb = map_shared_to_rank(fb_local, 0);
           uint8_t* sa = smem + stage * C::kStageBytes;
           uint8_t* sb = sa + C::kABytes;
           const int k0 = kb * C::BK;
-          tma_load_2d_pair(smem_u32(sa), &p.tmap_a, fb, k0, arow);
+          tma_load_2d_pair(smem_u32(sa), half ? &p.tmap_a2 : &p.tmap_a, fb, k0, arow);
           if (kBMnMajor) {
 #pragma unroll
             for (int c = 0; c < C::BN_CTA / 64; ++c)
@@ -162,14 +186,17 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_pair_kernel(const __grid_cons
       uint32_t phase = 0;
       bool ok = true;
       int local = 0;
+      int g = 0;
       for (int tile = pair; ok && tile < total_tiles; tile += num_pairs, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
-        if (!mbar_wait(smem_u32(tempty_bar + acc), acc_phase ^ 1, abort_flag)) break;
+        const Tile t = decode_tile<C::BM, C::BN>(tv, n_tiles, tile, g);
+        const uint32_t idesc = (halves && t.rows <= C::BM_CTA) ? C::kIdescHalf : C::kIdesc;
+        if (!mbar_wait(smem_u32(tempty_bar + acc), acc_phase ^ 1, abort_flag, wait_ns)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * C::BN;
         for (int kb = 0; kb < k_blocks; ++kb) {
-          if (!mbar_wait(smem_u32(full_bar + stage), phase, abort_flag)) {
+          if (!mbar_wait(smem_u32(full_bar + stage), phase, abort_flag, wait_ns)) {
             ok = false;
             break;
           }
@@ -182,7 +209,7 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_pair_kernel(const __grid_cons
             const uint64_t bdesc = kBMnMajor
                                        ? make_sw128_desc(sb + ks * C::kUmmaK * 128, C::BK * 128, 1024)
                                        : make_sw128_desc(sb + ks * 32, 16, 1024);
-            mma_f16_pair(d_tmem, adesc, bdesc, C::kIdesc, (kb | ks) != 0 ? 1u : 0u);
+            mma_f16_pair(d_tmem, adesc, bdesc, idesc, (kb | ks) != 0 ? 1u : 0u);
           }
           mma_commit_pair_mc(smem_u32(empty_bar + stage), 0x3);
           if (++stage == C::kStages) {
@@ -207,19 +234,30 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_pair_kernel(const __grid_cons
     for (int tile = pair; tile < total_tiles; tile += num_pairs, ++local) {
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
-      if (!mbar_wait(smem_u32(tfull_bar + acc), acc_phase, abort_flag)) break;
+      if (!mbar_wait(smem_u32(tfull_bar + acc), acc_phase, abort_flag, wait_ns)) break;
       tc_fence_after();
       const Tile t = decode_tile<C::BM, C::BN>(tv, n_tiles, tile, g);
-      const int rows_cta = t.rows - C::BM_CTA * static_cast<int>(cta);
-      const int row0 = t.row0 + C::BM_CTA * static_cast<int>(cta);
-      if (quarter * 32 < rows_cta) {  // warp-uniform
-        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * C::BN;
-        if (p.act)
-          drain_slab_swiglu<OutT>(p, tv, g, row0 + quarter * 32, min(32, rows_cta - quarter * 32),
-                                  t.n0 >> 1, taddr, stage, lane);
-        else
-          drain_slab<OutT, C::BN>(p, tv, g, row0 + quarter * 32, min(32, rows_cta - quarter * 32), t.n0,
-                                  taddr, stage, lane);
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * C::BN;
+      if (halves && t.rows <= C::BM_CTA) {
+        // half tile: this CTA holds rows [64 cta, 64 cta + 64) of the tile;
+        // warp q drains rows 32 (q & 1) .. +31 of output columns 128 (q >> 1) .. +127
+        const int rows_cta = t.rows - (C::BM_CTA / 2) * static_cast<int>(cta);
+        const int rb = (quarter & 1) * 32;
+        if (rb < rows_cta)  // warp-uniform
+          drain_slab<OutT, C::BN / 2>(p, tv, g, t.row0 + (C::BM_CTA / 2) * static_cast<int>(cta) + rb,
+                                      min(32, rows_cta - rb), t.n0 + (quarter >> 1) * (C::BN / 2), taddr,
+                                      stage, lane);
+      } else {
+        const int rows_cta = t.rows - C::BM_CTA * static_cast<int>(cta);
+        const int row0 = t.row0 + C::BM_CTA * static_cast<int>(cta);
+        if (quarter * 32 < rows_cta) {  // warp-uniform
+          if (p.act)
+            drain_slab_swiglu<OutT>(p, tv, g, row0 + quarter * 32, min(32, rows_cta - quarter * 32),
+                                    t.n0 >> 1, taddr, stage, lane);
+          else
+            drain_slab<OutT, C::BN>(p, tv, g, row0 + quarter * 32, min(32, rows_cta - quarter * 32), t.n0,
+                                    taddr, stage, lane);
+        }
       }
       tc_fence_before();
       __syncwarp();

@@ -90,6 +90,13 @@ struct __align__(64) GmmParams {
   int vk_m;        // variable-K kernel: rows of each D[e] (= columns of A)
   int vk_m_tiles;  // variable-K kernel: 128-row tiles per D[e]
   int ep_rank_base;  // remote mode: segment j of a group comes from rank (ep_rank_base + j) % world
+  // Bounded waits: limit of every pipeline wait (0 = kWaitTimeoutNs).  Test
+  // hook of the timeout path: drop_kb1 = k + 1 > 0 makes the producer(s) of
+  // the first tile of CTA (pair) 0 skip the loads of k-block k, so that the
+  // MMA warp's wait for them runs out (gmm_sm100_forward_inject_timeout);
+  // 0 (the zeroed default) drops nothing.
+  unsigned long long wait_ns;
+  int drop_kb1;
   void* d_peer[kMaxPeers];  // each rank's output buffer (remote mode)
   // Table of the non-empty groups, laid out as
   //   row_off[G+1] | tile_off[G+1] | expert[G] [| src_off[G][W+1] | dst_row[G][W]]
@@ -486,6 +493,7 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_persistent_kernel(const __gri
 
   const int n_tiles = p.n_tiles;
   const int k_blocks = p.k_blocks;
+  const unsigned long long wait_ns = p.wait_ns ? p.wait_ns : kWaitTimeoutNs;
   int num_groups = p.num_groups, total_tiles = p.total_tiles;
   const int32_t* tab = p.ext_table ? p.ext_table : p.inline_table;
   if (p.dev_bs) {
@@ -511,9 +519,16 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_persistent_kernel(const __gri
       for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
         const Tile t = decode_tile<C::BM, C::BN>(tv, n_tiles, tile, g);
         for (int kb = 0; kb < k_blocks; ++kb) {
-          if (!mbar_wait(smem_u32(empty_bar + stage), phase ^ 1, abort_flag)) {
+          if (!mbar_wait(smem_u32(empty_bar + stage), phase ^ 1, abort_flag, wait_ns)) {
             ok = false;
             break;
+          }
+          if (kb + 1 == p.drop_kb1 && tile == 0) {  // timeout test hook: this stage never fills
+            if (++stage == C::kStages) {
+              stage = 0;
+              phase ^= 1;
+            }
+            continue;
           }
           const uint32_t fb = smem_u32(full_bar + stage);
           mbar_arrive_expect_tx(fb, C::kStageBytes);
@@ -563,11 +578,11 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_persistent_kernel(const __gri
       for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
-        if (!mbar_wait(smem_u32(tempty_bar + acc), acc_phase ^ 1, abort_flag)) break;
+        if (!mbar_wait(smem_u32(tempty_bar + acc), acc_phase ^ 1, abort_flag, wait_ns)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * C::BN;
         for (int kb = 0; kb < k_blocks; ++kb) {
-          if (!mbar_wait(smem_u32(full_bar + stage), phase, abort_flag)) {
+          if (!mbar_wait(smem_u32(full_bar + stage), phase, abort_flag, wait_ns)) {
             ok = false;
             break;
           }
@@ -617,7 +632,7 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_persistent_kernel(const __gri
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++local) {
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
-      if (!mbar_wait(smem_u32(tfull_bar + acc), acc_phase, abort_flag)) break;
+      if (!mbar_wait(smem_u32(tfull_bar + acc), acc_phase, abort_flag, wait_ns)) break;
       tc_fence_after();
       const Tile t = decode_tile<C::BM, C::BN>(tv, n_tiles, tile, g);
       if (quarter * 32 < t.rows) {  // warp-uniform: some row of this quarter is live
@@ -773,6 +788,40 @@ __global__ void __launch_bounds__(256) ep_gather_kernel(const __grid_constant__ 
       dst[i + 96] = v3;
     }
     for (; i < n16; i += 32) dst[i] = src[i];
+  }
+}
+
+// ------------------------------------------------------------ expert-parallel barrier
+struct BarrierParams {
+  int* flags[kMaxPeers];  // each rank's flag slots (peer-accessible), flags[s][r] = last epoch rank r posted to s
+  int world;
+  int rank;
+  int epoch;
+  unsigned long long timeout_ns;
+};
+
+// Cross-rank barrier over peer memory, one thread per rank: thread s posts
+// this rank's epoch into rank s's slot for us (release, system scope: every
+// write this rank made earlier in the stream, its peer stores included, is
+// visible to s before the flag), then waits until rank s has posted the same
+// epoch here (acquire).  The wait is bounded: past timeout_ns it records
+// GMM_ERR_DEVICE_TIMEOUT in the device error word and returns.
+__global__ void __launch_bounds__(32) ep_barrier_kernel(const __grid_constant__ BarrierParams p) {
+  const int s = threadIdx.x;
+  if (s >= p.world) return;
+  __threadfence_system();
+  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p.flags[s] + p.rank), "r"(p.epoch) : "memory");
+  const int* mine = p.flags[p.rank] + s;
+  const unsigned long long t0 = global_timer_ns();
+  while (true) {
+    int v;
+    asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
+    if (v - p.epoch >= 0) break;  // epochs only grow; the difference is wrap-safe
+    if (global_timer_ns() - t0 > p.timeout_ns) {
+      atomicCAS(&g_device_error, 0, GMM_ERR_DEVICE_TIMEOUT);
+      break;
+    }
+    __nanosleep(64);
   }
 }
 
@@ -1135,6 +1184,10 @@ int setup_and_launch(GmmParams& prm, const void* A, const void* B, uint8_t* ws, 
     const cuuint64_t adims[2] = {uK, uT}, astr[1] = {uK * 2};
     const cuuint32_t abox[2] = {64, 128};
     if ((rc = encode(&prm.tmap_a, tt, 2, A, adims, astr, abox))) return rc;
+    if (tile_rows == 256) {  // half tiles of the CTA-pair kernel: 64 A rows per CTA
+      const cuuint32_t abox_half[2] = {64, 64};
+      if ((rc = encode(&prm.tmap_a2, tt, 2, A, adims, astr, abox_half))) return rc;
+    }
     if (trans_b) {  // B[e] is [N, K], K contiguous; a CTA of a pair holds half the tile's columns
       const cuuint64_t bdims[3] = {uK, uN, uE}, bstr[2] = {uK * 2, uN * uK * 2};
       const cuuint32_t bbox[3] = {64, (tile_rows == 256 || act) ? 128u : 256u, 1};
@@ -1197,10 +1250,17 @@ int plan_impl(const int64_t* batch_sizes, int64_t num_experts, int64_t num_token
   return GMM_OK;
 }
 
+// Test hook of the bounded-wait path (gmm_sm100_forward_inject_timeout).
+struct InjectTimeout {
+  int drop_k_block;
+  unsigned long long wait_ns;
+};
+
 // The device half: argument checks that need the pointers, tensor maps, launch.
 // `pl` is the plan's table (with the expert-parallel segments appended in EP mode).
 int launch_impl(const PlanObj& po, const Plan& pl, const void* A, const void* B, void* D, void* workspace,
-                size_t workspace_bytes, void* stream_ptr, const EpRoute* ep, int act) {
+                size_t workspace_bytes, void* stream_ptr, const EpRoute* ep, int act,
+                const InjectTimeout* inject = nullptr) {
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
   int rc = GMM_OK;
   const TileKind kind = po.kind;
@@ -1262,6 +1322,10 @@ int launch_impl(const PlanObj& po, const Plan& pl, const void* A, const void* B,
   prm.act = act;
   prm.act_cols = act ? static_cast<int>(N_out) : 0;
   prm.tile_rows = static_cast<int>(tile_rows);
+  if (inject) {
+    prm.drop_kb1 = inject->drop_k_block + 1;
+    prm.wait_ns = inject->wait_ns;
+  }
   if (ep) {
     prm.remote = 1;
     prm.world = ep->world;
@@ -1461,6 +1525,26 @@ int gmm_sm100_ep_gather(void* X, const void* const* src_peers, const int64_t* co
   return ce == cudaSuccess ? GMM_OK : cuda_fail(ce, "ep gather launch");
 }
 
+int gmm_sm100_ep_barrier(int* const* flag_peers, int world, int rank, int epoch, double timeout_s,
+                         void* stream_ptr) {
+  if (!flag_peers || world < 1 || world > kMaxPeers || rank < 0 || rank >= world || !(timeout_s > 0.0))
+    return fail(GMM_ERR_INVALID_ARGUMENT, "bad barrier arguments");
+  BarrierParams prm;
+  std::memset(&prm, 0, sizeof(prm));
+  for (int s = 0; s < world; ++s) {
+    if (!flag_peers[s] || (reinterpret_cast<uintptr_t>(flag_peers[s]) & 3u))
+      return fail(GMM_ERR_ALIGNMENT, "every rank's flag slots must be non-null and 4-byte aligned");
+    prm.flags[s] = flag_peers[s];
+  }
+  prm.world = world;
+  prm.rank = rank;
+  prm.epoch = epoch;
+  prm.timeout_ns = static_cast<unsigned long long>(std::min(timeout_s, 3600.0) * 1e9);
+  ep_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream_ptr)>>>(prm);
+  const cudaError_t ce = cudaGetLastError();
+  return ce == cudaSuccess ? GMM_OK : cuda_fail(ce, "ep barrier launch");
+}
+
 int gmm_sm100_forward_swiglu(const void* A, const void* B, const int64_t* batch_sizes, int64_t num_experts,
                              int64_t num_tokens, int64_t dim, int64_t dim_out, int dtype, int trans_b,
                              void* D, void* workspace, size_t workspace_bytes, void* stream) {
@@ -1623,6 +1707,25 @@ int gmm_sm100_forward_vark(const void* A, const void* B, const int64_t* batch_si
   };
   return dtype == GMM_DTYPE_BF16 ? launch(gmm_vark_kernel<kKindBf16>, VarKCfg<kKindBf16>::kSmemBytes)
                                  : launch(gmm_vark_kernel<kKindF16>, VarKCfg<kKindF16>::kSmemBytes);
+}
+
+int gmm_sm100_forward_inject_timeout(const void* A, const void* B, const int64_t* batch_sizes,
+                                     int64_t num_experts, int64_t num_tokens, int64_t dim, int64_t dim_out,
+                                     int dtype, int trans_b, void* D, int drop_k_block, double wait_s,
+                                     void* stream) {
+  if (dtype != GMM_DTYPE_BF16 && dtype != GMM_DTYPE_F16)
+    return fail(GMM_ERR_DTYPE, "the timeout test hook runs the 16-bit kernels");
+  if (!(wait_s > 0.0 && wait_s <= 2.0) || drop_k_block < 0)
+    return fail(GMM_ERR_INVALID_ARGUMENT, "wait_s must be in (0, 2] and drop_k_block >= 0");
+  PlanObj po;
+  int rc = plan_impl(batch_sizes, num_experts, num_tokens, dim, dim_out, dtype, trans_b, 0, false, po);
+  if (rc != GMM_OK) return rc;
+  if (po.kind == kTileSwap)
+    return fail(GMM_ERR_INVALID_ARGUMENT, "the timeout test hook runs the 128-row and CTA-pair kernels");
+  if (po.pl.table_bytes != 0 || drop_k_block >= po.pl.k_blocks || po.pl.total_tiles == 0)
+    return fail(GMM_ERR_INVALID_ARGUMENT, "the timeout test hook needs a small problem with that k-block");
+  const InjectTimeout inj{drop_k_block, static_cast<unsigned long long>(wait_s * 1e9)};
+  return launch_impl(po, po.pl, A, B, D, nullptr, 0, stream, nullptr, 0, &inj);
 }
 
 int gmm_sm100_device_error(int* status_out, int clear) {

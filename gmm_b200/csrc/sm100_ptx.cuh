@@ -55,8 +55,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Wait until the phase with parity `parity` of `bar` has completed.  Returns
-// false (and raises *abort) if the CTA was aborted or the wait timed out.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+// false (and raises *abort) if the CTA was aborted or the wait ran longer
+// than timeout_ns.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                          unsigned long long timeout_ns = kWaitTimeoutNs) {
 #pragma unroll 1
   for (int i = 0; i < 32; ++i)
     if (mbar_try_wait(bar, parity)) return true;
@@ -65,7 +67,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+    if (global_timer_ns() - t0 > timeout_ns) {
       *abort_flag = 1;
       return false;
     }

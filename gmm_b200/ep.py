@@ -32,10 +32,14 @@ Two transports carry steps 2 and 4:
   receive buffer with peer loads; the combine is fused into the grouped-GEMM
   epilogue, which stores each result row straight into the output buffer of
   the rank it came from, tile by tile, while the next tiles are computed.
-  Two 1-element NCCL all-reduces on the compute stream order the step: inputs
-  written everywhere before the gather, all peer stores landed before the
-  output is read.  The returned tensor is a view of this rank's symmetric
-  output buffer, valid until the next call.
+  Two cross-rank barriers order the step: inputs written everywhere before
+  the gather, all peer stores landed before the output is read.  By default
+  they are one small kernel each over symmetric-memory flags
+  (``gmm_sm100_ep_barrier``: release/acquire at system scope, bounded wait);
+  ``barrier="nccl"`` uses 1-element NCCL all-reduces instead.  The result is
+  copied out of the symmetric output buffer into ``out`` (a new tensor by
+  default); passing ``out=layer.output_buffer(...)`` skips that copy, and the
+  result is then overwritten by the next call.
 * ``"nccl"``: NCCL point-to-point messages (below); also what the CPU tests
   run on gloo ranks.
 
@@ -107,14 +111,23 @@ class ExpertParallelGmm:
         count_exchange: ``"shm"`` (shared memory, ranks on one host), ``"gloo"``, or
             ``"auto"`` (shm when every rank is on this host).  Construction is
             collective over the count group.
+        barrier: cross-rank barrier of the direct transport: ``"flags"`` (one small
+            kernel over symmetric-memory flags) or ``"nccl"`` (1-element all-reduce).
     """
 
     def __init__(self, num_experts: int, group=None, count_group=None,
                  local_gemm: Optional[Callable] = None, chunks: int = 1, transport: str = "auto",
-                 count_exchange: str = "auto"):
+                 count_exchange: str = "auto", barrier: str = "flags"):
         if transport not in ("auto", "direct", "nccl"):
             raise ValueError(f"unknown transport {transport!r}")
+        if barrier not in ("flags", "nccl"):
+            raise ValueError(f"unknown barrier {barrier!r}")
         self.transport = transport
+        self.barrier = barrier
+        self._epoch = 0
+        self._flags = None  # (symmetric int32 flag slots, their per-rank addresses, handle)
+        self.record_phases = False  # when set, CUDA events around each phase of a direct step
+        self.phase_events = []
         self._sym = None  # (capacity rows, dim, dim_out, dtype, device, a_sym, out_sym, a_ptrs, out_ptrs)
         self._flag = None
         self.group = group
@@ -184,9 +197,24 @@ class ExpertParallelGmm:
         return ok
 
     def _barrier(self, device):
-        if self._flag is None or self._flag.device != device:
-            self._flag = torch.zeros(1, dtype=torch.float32, device=device)
-        dist.all_reduce(self._flag, group=self.group)
+        if self.barrier == "nccl":
+            if self._flag is None or self._flag.device != device:
+                self._flag = torch.zeros(1, dtype=torch.float32, device=device)
+            dist.all_reduce(self._flag, group=self.group)
+            return
+        from gmm_b200 import capi
+        if self._flags is None or self._flags[0].device != device:
+            import torch.distributed._symmetric_memory as symm_mem
+            group = self.group if self.group is not None else dist.group.WORLD
+            f = symm_mem.empty(8, dtype=torch.int32, device=device)
+            f.zero_()
+            h = symm_mem.rendezvous(f, group)
+            torch.cuda.synchronize(device)
+            dist.barrier(group=self.count_group)  # every rank's slots are zero before any post
+            self._flags = (f, list(h.buffer_ptrs), h)
+            self._epoch = 0
+        self._epoch += 1
+        capi.ep_barrier(self._flags[1], self.rank, self._epoch, device)
 
     def _symmetric(self, rows: int, dim: int, dim_out: int, dtype, device):
         """(Re)allocate the symmetric token / output buffers; collective when it allocates.
@@ -217,7 +245,22 @@ class ExpertParallelGmm:
         sym = self._symmetric(rows, dim, dim_out, dtype, device)
         return sym[5][:rows * dim].view(rows, dim)
 
-    def _forward_direct(self, a, b_local, all_bs, trans_b):
+    def output_buffer(self, rows: int, dim: int, dim_out: int, dtype, device) -> torch.Tensor:
+        """A ``[rows, dim_out]`` view of this rank's symmetric output buffer.
+
+        Passed as ``out=``, the result is left where the peers' epilogues
+        stored it (no copy); it is then valid only until the next call.
+        Collective like ``input_buffer``."""
+        sym = self._symmetric(rows, dim, dim_out, dtype, device)
+        return sym[6][:rows * dim_out].view(rows, dim_out)
+
+    def _mark(self, device):
+        if self.record_phases:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record(torch.cuda.current_stream(device))
+            self.phase_events.append(e)
+
+    def _forward_direct(self, a, b_local, all_bs, trans_b, out=None):
         from gmm_b200 import capi
         W, El, r = self.world, self.e_local, self.rank
         dim = a.shape[1]
@@ -225,7 +268,7 @@ class ExpertParallelGmm:
         rows_max = int(all_bs.sum(1).max())
         sym = self._symmetric(rows_max, dim, dim_out, a.dtype, a.device)
         a_sym = sym[5][:a.shape[0] * dim].view(a.shape[0], dim)
-        out = sym[6][:a.shape[0] * dim_out].view(a.shape[0], dim_out)
+        res = sym[6][:a.shape[0] * dim_out].view(a.shape[0], dim_out)
         if a.data_ptr() != a_sym.data_ptr():
             a_sym.copy_(a)
         # offsets of every global expert's rows in every rank's layout: [W, E]
@@ -239,16 +282,39 @@ class ExpertParallelGmm:
         rows_at = offs[order][:, mine].t().contiguous().numpy()   # where they sit on their rank
         n_recv = int(counts.sum())
         x = self._buffer("_x", n_recv, dim, a)
+        if self.record_phases:
+            self.phase_events = []
+        self._mark(a.device)
         self._barrier(a.device)  # every rank's token rows are in place
+        self._mark(a.device)
         if n_recv:
             capi.ep_gather(x, sym[7], counts, rows_at, El, dim * a.element_size(), rank_base=r)
+            self._mark(a.device)
             capi.forward_ep(x, b_local, counts, rows_at, El, sym[8], trans_b=trans_b, rank_base=r)
+        else:
+            self._mark(a.device)
+        self._mark(a.device)
         self._barrier(a.device)  # every peer's result rows have landed here
+        self._mark(a.device)
+        if out is None:
+            return res.clone()
+        if out.data_ptr() != res.data_ptr():
+            out.copy_(res)
         return out
+
+    def phase_ms(self):
+        """Milliseconds of the last direct step's phases (``record_phases`` must
+        have been set): barrier before, gather, GEMM + combine, barrier after."""
+        ev = self.phase_events
+        if len(ev) != 5:
+            return None
+        return {name: ev[i].elapsed_time(ev[i + 1])
+                for i, name in enumerate(("barrier_in", "gather", "gemm_combine", "barrier_out"))}
 
     # --------------------------------------------------------------- forward
     def forward(self, a: torch.Tensor, b_local: torch.Tensor, batch_sizes: torch.Tensor,
-                trans_b: bool = False, all_bs: Optional[torch.Tensor] = None) -> torch.Tensor:
+                trans_b: bool = False, all_bs: Optional[torch.Tensor] = None,
+                out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """``out[rows_g] = a[rows_g] @ B[g]`` for this rank's rows, with B sharded by expert.
 
         Args:
@@ -257,6 +323,8 @@ class ExpertParallelGmm:
                 weights of the experts this rank owns.
             batch_sizes: ``[E]`` CPU int64, this rank's rows per global expert.
             all_bs: the gathered ``[W, E]`` counts, if the caller already has them.
+            out: ``[T_r, dim_out]`` tensor for the result (default: a new tensor);
+                ``output_buffer(...)`` avoids the copy out of symmetric memory.
         """
         W, El, r = self.world, self.e_local, self.rank
         if a.dim() != 2 or b_local.dim() != 3 or b_local.shape[0] != El:
@@ -267,8 +335,11 @@ class ExpertParallelGmm:
                              f"A.size(0) ({a.shape[0]})")
         if all_bs is None:
             all_bs = self.exchange_counts(batch_sizes)
+        if out is not None and (tuple(out.shape) != (a.shape[0], b_local.shape[1] if trans_b else b_local.shape[2])
+                                or out.dtype != a.dtype or out.device != a.device):
+            raise ValueError("out must be a [T_r, dim_out] tensor of a's dtype and device")
         if self._use_direct(a):
-            return self._forward_direct(a, b_local, all_bs, trans_b)
+            return self._forward_direct(a, b_local, all_bs, trans_b, out)
         bs = all_bs.tolist()
         ch = _Chunking(bs, W, El, self.chunks)
         C = ch.chunks
@@ -291,7 +362,8 @@ class ExpertParallelGmm:
         n_recv = off
         x = self._buffer("_x", n_recv, dim, a)
         y = self._buffer("_y", n_recv, dim_out, a)
-        out = torch.empty(a.shape[0], dim_out, dtype=a.dtype, device=a.device)
+        if out is None:
+            out = torch.empty(a.shape[0], dim_out, dtype=a.dtype, device=a.device)
 
         # ---- dispatch: all batches posted up front, one per chunk
         pending = []

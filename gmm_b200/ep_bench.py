@@ -1,20 +1,30 @@
-"""Expert-parallel leg of ``bench.py`` (one process per GPU, launched by torchrun).
+"""Expert-parallel leg of ``bench.py`` (one process per GPU, launched by torchrun),
+and the in-run parity check both legs use.
 
-Workloads (``--config``):
+Headline workload (``--config``, default 2): cfg2 shapes, weak scaling -- every
+rank routes 8192 tokens (top-2 over the 8 experts) and owns E/N experts; at
+N = 1 this is exactly the single-GPU cfg2 workload.  ``--config 5`` / ``3``
+make cfg5 / cfg3 the headline instead (strong scaling).
 
-* 2 (default): cfg2 shapes, weak scaling -- every rank routes 8192 tokens
-  (top-2 over the 8 experts) and owns E/N experts; at N = 1 this is exactly
-  the single-GPU cfg2 workload.
-* 5: cfg5 (Mixtral-8x22B shapes), strong scaling -- 32768 tokens in total,
-  split evenly over the ranks; 8/N experts per rank.
-* 3: cfg3 (DeepSeek-V3 shapes, fp16 NT), strong scaling -- 4096 tokens in total,
-  256/N experts per rank.
+Every N also reports ``ep_configs``: the two expert-parallel configurations
+of the north star, strong-scaled --
 
-A step is the host count exchange + NCCL dispatch + local grouped GEMM +
-NCCL combine (``gmm_b200.ep.ExpertParallelGmm``).  Time is measured with CUDA
-events on each rank's stream between barriers and reduced with MAX over the
-ranks; ``value`` is whole-job FLOPs per second, ``tokens_per_s`` pre-top-k
-tokens per second.
+* cfg5 (Mixtral-8x22B shapes, bf16 NN): 32768 tokens in total, split evenly
+  over the ranks; 8/N experts per rank;
+* cfg3 (DeepSeek-V3 shapes, fp16 NT): 4096 tokens in total, 256/N experts
+  per rank --
+
+each with its step time, tokens/s, whole-job TFLOP/s, the load-imbalance
+ceiling of its routing (mean / max rows computed per rank) and ``parity``:
+sampled output rows of every rank, two or more per global expert (so every
+rank's local experts are covered), against a plain PyTorch fp32 reference on
+the GPU at the north-star tolerance.
+
+A step is the count exchange + dispatch + local grouped GEMM + combine
+(``gmm_b200.ep.ExpertParallelGmm``, direct transport: NVLink peer-load gather,
+combine fused into the GEMM epilogue, flag barriers).  Time is measured with
+CUDA events on each rank's stream between barriers and reduced with MAX over
+the ranks.
 """
 
 from __future__ import annotations
@@ -23,39 +33,197 @@ import datetime
 import json
 import math
 import os
-import statistics
 
 import torch
 import torch.distributed as dist
 
 
-def _routing(cfg, world, rank):
+# ------------------------------------------------------------------ parity
+def check_parity(out, a, bs, get_b, trans_b, rows_per_expert=2, seed=0, max_experts=None):
+    """Sampled rows of ``out`` (grouped by expert per ``bs``) against a plain
+    PyTorch fp32 matmul on the GPU, rounded to the output dtype.
+
+    For every non-empty expert g (or the first ``max_experts`` of them) its first
+    and last row and ``rows_per_expert`` random rows are checked against
+    ``a[rows].float() @ B[g].float()`` with ``B[g] = get_b(g)``; tolerance
+    rtol = atol from the north star (bf16 1.6e-2, fp16 2e-3, fp32 5e-3).
+    Returns a JSON-ready summary."""
+    from gmm_b200.configs import TOLERANCE
+    tol = TOLERANCE[out.dtype]
+    g = torch.Generator().manual_seed(seed)
+    bsl = [int(v) for v in bs]
+    off = 0
+    n_rows = n_bad = n_exp = 0
+    max_err = 0.0
+    prev_tf32 = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        for e, m in enumerate(bsl):
+            if m > 0 and (max_experts is None or n_exp < max_experts):
+                rows = {off, off + m - 1}
+                rows.update(int(v) for v in torch.randint(off, off + m, (rows_per_expert,), generator=g))
+                idx = torch.tensor(sorted(rows), device=out.device)
+                b = get_b(e).float()
+                want = a[idx].float() @ (b.t() if trans_b else b)
+                want = want.to(out.dtype).float()
+                got = out[idx].float()
+                err = (got - want).abs()
+                n_bad += int((err > tol + tol * want.abs()).sum())
+                if not torch.isfinite(got).all():
+                    n_bad += 1
+                max_err = max(max_err, float(err.max()))
+                n_rows += len(rows)
+                n_exp += 1
+            off += m
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev_tf32
+    return {"ok": n_bad == 0, "rows": n_rows, "experts": n_exp, "bad_elements": n_bad,
+            "max_abs_err": max_err, "tol": tol,
+            "reference": "torch fp32 matmul on the GPU (TF32 off), rounded to the output dtype"}
+
+
+# ------------------------------------------------------------------ workloads
+def routing(cfg, world, rank, weak):
     """This rank's token shard of one global routing draw (same on every rank)."""
     from gmm_b200.configs import route
-    weak = cfg.cid == 2
     tokens_r = cfg.tokens if weak else cfg.tokens // world
     total = tokens_r * world
     gen = torch.Generator().manual_seed(cfg.seed)
     ids = route(cfg, gen, tokens=total)
-    mine = ids[rank * tokens_r:(rank + 1) * tokens_r]
-    bs = torch.bincount(mine.flatten(), minlength=cfg.num_experts).to(torch.int64)
-    return bs, tokens_r, total, weak
+    bs_all = [torch.bincount(ids[r * tokens_r:(r + 1) * tokens_r].flatten(),
+                             minlength=cfg.num_experts).to(torch.int64) for r in range(world)]
+    return bs_all[rank], tokens_r, total, torch.stack(bs_all)
 
 
-def _local_weights(cfg, experts, device):
+def expert_weight(cfg, e, device):
+    """B[e] of the expert-parallel workloads: its own seeded draw, so any rank can
+    regenerate any expert's weights (the parity check does)."""
     from gmm_b200.configs import b_shape
-    shape = b_shape(cfg, len(experts))
-    b = torch.empty(*shape, dtype=cfg.dtype, device=device)
-    s = 1.0 / math.sqrt(cfg.dim)
+    shape = b_shape(cfg, 1)[1:]
+    gen = torch.Generator(device=device).manual_seed(cfg.seed * 100003 + e)
+    w = torch.randn(*shape, generator=gen, device=device).mul_(1.0 / math.sqrt(cfg.dim))
+    return w.to(cfg.dtype)
+
+
+def local_weights(cfg, experts, device):
+    from gmm_b200.configs import b_shape
+    b = torch.empty(*b_shape(cfg, len(experts)), dtype=cfg.dtype, device=device)
     for i, e in enumerate(experts):
-        g = torch.Generator(device=device).manual_seed(cfg.seed * 100003 + e)
-        b[i].copy_(torch.randn(*shape[1:], generator=g, device=device).mul_(s))
+        b[i].copy_(expert_weight(cfg, e, device))
     return b
 
 
+def _dtype_name(dtype):
+    return {torch.bfloat16: "bf16", torch.float16: "fp16", torch.float32: "fp32"}[dtype]
+
+
+def _max_over_ranks(v, dev):
+    t = torch.tensor([float(v)], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.item()
+
+
+def _sum_over_ranks(v, dev):
+    t = torch.tensor([float(v)], dtype=torch.float64, device=dev)
+    dist.all_reduce(t)
+    return t.item()
+
+
+class _Setup:
+    """One expert-parallel workload on this rank: routing, weights, inputs, layer."""
+
+    def __init__(self, cfg, world, rank, dev, count_group, weak, barrier="flags"):
+        from gmm_b200.ep import ExpertParallelGmm
+        self.cfg, self.world, self.rank, self.dev = cfg, world, rank, dev
+        E = cfg.num_experts
+        if E % world:
+            raise SystemExit(f"cfg{cfg.cid}: {E} experts do not split over {world} ranks")
+        self.El = El = E // world
+        self.bs, self.tokens_r, self.tokens_total, all_bs = routing(cfg, world, rank, weak)
+        self.rows_r = int(self.bs.sum())
+        self.b_local = local_weights(cfg, list(range(rank * El, (rank + 1) * El)), dev)
+        self.ep = ExpertParallelGmm(E, count_group=count_group,
+                                    transport=os.environ.get("GMM_EP_TRANSPORT", "auto"), barrier=barrier)
+        self.all_bs = self.ep.exchange_counts(self.bs)
+        assert torch.equal(self.all_bs, all_bs), "count exchange disagrees with the routing draw"
+        g = torch.Generator(device=dev).manual_seed(cfg.seed * 7919 + rank)
+        cap = int(self.all_bs.sum(1).max())
+        self.direct = self.ep._use_direct(self.b_local)
+        if self.direct:
+            # the layer's input rows live in this rank's symmetric token buffer and
+            # its result stays in the symmetric output buffer (no copies)
+            self.a = self.ep.input_buffer(cap, cfg.dim, cfg.dim_out, cfg.dtype, dev)[:self.rows_r]
+            self.a.copy_(torch.randn(self.rows_r, cfg.dim, generator=g, device=dev))
+            self.out = self.ep.output_buffer(cap, cfg.dim, cfg.dim_out, cfg.dtype, dev)[:self.rows_r]
+        else:
+            self.a = torch.randn(self.rows_r, cfg.dim, generator=g, device=dev).to(cfg.dtype)
+            self.out = torch.empty(self.rows_r, cfg.dim_out, dtype=cfg.dtype, device=dev)
+        self.rows_total = _sum_over_ranks(self.rows_r, dev)
+        self.flops = 2.0 * self.rows_total * cfg.dim * cfg.dim_out
+        # rows each rank's GEMM computes: every rank's rows for its local experts
+        per_rank = self.all_bs.view(world, world, El).sum(dim=(0, 2)).double()
+        self.imbalance = {"rows_per_rank_max": int(per_rank.max()), "rows_per_rank_mean": float(per_rank.mean()),
+                          "efficiency_ceiling": round(float(per_rank.mean() / per_rank.max()), 4)}
+
+    def step(self):
+        return self.ep(self.a, self.b_local, self.bs, self.cfg.trans_b, all_bs=self.all_bs, out=self.out)
+
+    def timed(self, steps, warmup):
+        for _ in range(max(3, warmup)):
+            self.step()
+        torch.cuda.synchronize()
+        stream = torch.cuda.current_stream()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        dist.barrier()
+        torch.cuda.synchronize()
+        t0.record(stream)
+        for _ in range(steps):
+            self.step()
+        t1.record(stream)
+        torch.cuda.synchronize()
+        return _max_over_ranks(t0.elapsed_time(t1) / steps, self.dev)
+
+    def parity(self):
+        """This rank's output rows (the last step's) for every global expert."""
+        cfg, El = self.cfg, self.El
+
+        def get_b(e):
+            if self.rank * El <= e < (self.rank + 1) * El:
+                return self.b_local[e - self.rank * El]
+            return expert_weight(cfg, e, self.dev)
+
+        res = check_parity(self.out, self.a, self.bs.tolist(), get_b, cfg.trans_b, seed=self.rank)
+        ok = _sum_over_ranks(0 if res["ok"] else 1, self.dev) == 0
+        return {"ok": ok, "rows_checked": int(_sum_over_ranks(res["rows"], self.dev)),
+                "max_abs_err": _max_over_ranks(res["max_abs_err"], self.dev), "tol": res["tol"],
+                "reference": res["reference"] + "; 2+ rows per (rank, global expert)"}
+
+    def phases(self):
+        if not self.direct:
+            return None
+        self.ep.record_phases = True
+        self.step()
+        torch.cuda.synchronize()
+        ph = self.ep.phase_ms()
+        self.ep.record_phases = False
+        return {k: round(_max_over_ranks(v, self.dev), 4) for k, v in ph.items()}
+
+    def close(self):
+        del self.a, self.out, self.b_local, self.ep
+        torch.cuda.empty_cache()
+
+
+def ep_config_entry(setup, ms, world):
+    cfg = setup.cfg
+    return {"workload": f"cfg{cfg.cid}: {cfg.name}", "dtype": _dtype_name(cfg.dtype),
+            "scaling": "strong", "tokens": setup.tokens_total, "experts_per_rank": setup.El,
+            "ms_per_step": round(ms, 4), "tokens_per_s": round(setup.tokens_total / (ms * 1e-3), 1),
+            "tflops": round(setup.flops / (ms * 1e-3) / 1e12, 2), "n_gpus": world,
+            "load_imbalance": setup.imbalance}
+
+
 def run(args, metric, load_peaks, clock_sampler):
-    from gmm_b200.configs import CONFIGS
-    from gmm_b200.ep import ExpertParallelGmm
+    from gmm_b200.configs import CONFIGS, workload_config
 
     # NCCL keeps P2P tensors alive until wait() instead of recording them on its
     # stream, so the allocator can reuse them at once on the compute stream.
@@ -70,30 +238,10 @@ def run(args, metric, load_peaks, clock_sampler):
     try:
         cid = args.config or 2
         cfg = CONFIGS[cid]
-        E = cfg.num_experts
-        if E % world:
-            raise SystemExit(f"cfg{cid}: {E} experts do not split over {world} ranks")
-        El = E // world
-        bs, tokens_r, tokens_total, weak = _routing(cfg, world, rank)
-        rows_r = int(bs.sum())
-        b_local = _local_weights(cfg, list(range(rank * El, (rank + 1) * El)), dev)
-        ep = ExpertParallelGmm(E, count_group=count_group,
-                               transport=os.environ.get("GMM_EP_TRANSPORT", "auto"))
-        all_bs = ep.exchange_counts(bs)
-        g = torch.Generator(device=dev).manual_seed(cfg.seed * 7919 + rank)
-        if ep._use_direct(b_local):
-            # the layer's input rows live in this rank's symmetric token buffer
-            a = ep.input_buffer(int(all_bs.sum(1).max()), cfg.dim, cfg.dim_out, cfg.dtype, dev)[:rows_r]
-            a.copy_(torch.randn(rows_r, cfg.dim, generator=g, device=dev))
-        else:
-            a = torch.randn(rows_r, cfg.dim, generator=g, device=dev).to(cfg.dtype)
-
-        rows_all = torch.tensor([rows_r], dtype=torch.float64, device=dev)
-        dist.all_reduce(rows_all)
-        flops = 2.0 * rows_all.item() * cfg.dim * cfg.dim_out
-
+        weak = cid == 2
+        s = _Setup(cfg, world, rank, dev, count_group, weak)
         for _ in range(max(3, args.warmup)):
-            ep(a, b_local, bs, cfg.trans_b)
+            s.step()
         torch.cuda.synchronize()
         stream = torch.cuda.current_stream()
         t0 = torch.cuda.Event(enable_timing=True)
@@ -105,25 +253,25 @@ def run(args, metric, load_peaks, clock_sampler):
             torch.cuda.synchronize()
             t0.record(stream)
             for _ in range(args.steps):
-                ep(a, b_local, bs, cfg.trans_b)
+                s.step()
             t1.record(stream)
             torch.cuda.synchronize()
-        ms = torch.tensor([t0.elapsed_time(t1) / args.steps], dtype=torch.float64, device=dev)
-        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-        step_ms = ms.item()
+        step_ms = _max_over_ranks(t0.elapsed_time(t1) / args.steps, dev)
+        head_parity = s.parity()
+        phases = s.phases() if args.phases else None
         dist.barrier()
 
-        # e2e: A_r and this rank's expert weights from pinned host memory, out back to host
-        a_h = a.cpu().pin_memory()
-        b_h = b_local.cpu().pin_memory()
-        a_d, b_d = a, torch.empty_like(b_local)  # inputs land where the layer reads them
-        out_h = torch.empty(rows_r, cfg.dim_out, dtype=cfg.dtype).pin_memory()
+        # e2e: A_r and this rank's expert weights from pinned host memory, result back to host
+        a_h = s.a.cpu().pin_memory()
+        b_h = s.b_local.cpu().pin_memory()
+        b_d = torch.empty_like(s.b_local)
+        out_h = torch.empty(s.rows_r, cfg.dim_out, dtype=cfg.dtype).pin_memory()
 
         def e2e_step():
-            a_d.copy_(a_h, non_blocking=True)
+            s.a.copy_(a_h, non_blocking=True)  # inputs land where the layer reads them
             b_d.copy_(b_h, non_blocking=True)
-            out = ep(a_d, b_d, bs, cfg.trans_b)
-            out_h.copy_(out, non_blocking=True)
+            o = s.ep(s.a, b_d, s.bs, cfg.trans_b, all_bs=s.all_bs, out=s.out)
+            out_h.copy_(o, non_blocking=True)
 
         e2e_step()
         torch.cuda.synchronize()
@@ -136,13 +284,30 @@ def run(args, metric, load_peaks, clock_sampler):
             e2e_step()
         e1.record(stream)
         torch.cuda.synchronize()
-        ems = torch.tensor([e0.elapsed_time(e1) / e_steps], dtype=torch.float64, device=dev)
-        dist.all_reduce(ems, op=dist.ReduceOp.MAX)
-        es = a.element_size()
-        h2d = torch.tensor([float((a.numel() + b_local.numel()) * es)], dtype=torch.float64, device=dev)
-        d2h = torch.tensor([float(rows_r * cfg.dim_out * es)], dtype=torch.float64, device=dev)
-        dist.all_reduce(h2d)
-        dist.all_reduce(d2h)
+        e2e_ms = _max_over_ranks(e0.elapsed_time(e1) / e_steps, dev)
+        es = s.a.element_size()
+        h2d = _sum_over_ranks((s.a.numel() + s.b_local.numel()) * es, dev)
+        d2h = _sum_over_ranks(s.rows_r * cfg.dim_out * es, dev)
+        head_imb = s.imbalance
+        transport = s.direct
+        shm = s.ep._shm_counts is not None
+        flops, tokens_total, rows_total, El = s.flops, s.tokens_total, s.rows_total, s.El
+        s.close()
+        del b_d, b_h, a_h
+
+        # the north star's expert-parallel configurations, strong-scaled
+        ep_configs = {}
+        if not args.no_configs:
+            for ecid in (5, 3):
+                es_ = _Setup(CONFIGS[ecid], world, rank, dev, count_group, weak=False)
+                ms = es_.timed(max(3, min(args.steps, 20)), args.warmup)
+                entry = ep_config_entry(es_, ms, world)
+                entry["parity"] = es_.parity()
+                if args.phases:
+                    entry["phases_ms"] = es_.phases()
+                ep_configs[f"cfg{ecid}"] = entry
+                es_.close()
+                dist.barrier()
 
         if rank == 0:
             peaks, src = load_peaks()
@@ -153,33 +318,32 @@ def run(args, metric, load_peaks, clock_sampler):
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 4),
                 "tokens_per_s": round(tokens_total / (step_ms * 1e-3), 1),
                 "higher_is_better": True, "scaling": "weak" if weak else "strong",
-                "vs_baseline": None,
-                "dtype": {torch.bfloat16: "bf16", torch.float16: "fp16", torch.float32: "fp32"}[cfg.dtype],
+                "vs_baseline": None, "dtype": _dtype_name(cfg.dtype),
                 "data": "synthetic (one seeded global routing draw, token-sharded; "
                         "A ~ N(0,1), B ~ N(0,1/dim))",
-                "config": {"workload": f"cfg{cid}: {cfg.name}, expert parallel",
-                           "experts": E, "experts_per_rank": El, "dim": cfg.dim,
-                           "dim_out": cfg.dim_out, "tokens": tokens_total, "top_k": cfg.top_k,
-                           "rows": int(rows_all.item()), "trans_b": cfg.trans_b,
-                           "parallelism": f"ep{world}",
-                           "l2": "inputs larger than L2 (126 MB)",
-                           "exchange": (("shared-memory" if ep._shm_counts is not None else "gloo")
-                                        + " count all-gather; "
-                                        + ("NVLink peer-load gather + combine fused into the GEMM "
-                                           "epilogue (symmetric memory)" if ep._use_direct(b_local)
-                                           else "NCCL P2P dispatch/combine"))},
-                "e2e": {"value": round(flops / (ems.item() * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
-                        "ms_per_step": round(ems.item(), 3),
-                        "h2d_bytes_per_step": int(h2d.item()), "d2h_bytes_per_step": int(d2h.item()),
+                "config": workload_config(cfg, world, weak),
+                "ep": {"experts_per_rank": El, "rows": int(rows_total),
+                       "exchange": (("shared-memory" if shm else "gloo") + " count all-gather; "
+                                    + ("NVLink peer-load gather + combine fused into the GEMM "
+                                       "epilogue (symmetric memory), flag barriers" if transport
+                                       else "NCCL P2P dispatch/combine")),
+                       "load_imbalance": head_imb},
+                "parity": head_parity,
+                "e2e": {"value": round(flops / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+                        "ms_per_step": round(e2e_ms, 3),
+                        "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                         "path": "pinned host A_r, B_local -> device; EP forward; out -> pinned host"},
-                "gpu_launches": args.steps * world,
+                "gpu_launches": args.steps * (4 if transport else 1),
                 "roofline": {"bound": "tensor", "achieved": round(per_gpu, 2),
                              "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                              "frac": round(per_gpu / peaks["bf16_tflops"], 4), "traffic": None,
                              "peak_source": f"{src} (burst); achieved = whole-job TFLOP/s / N, "
-                                            "including the NCCL exchange"},
+                                            "including the exchange"},
                 "clocks": clk.summary(),
+                "ep_configs": ep_configs,
             }
+            if phases:
+                line["phases_ms"] = phases
             print(json.dumps(line), flush=True)
     finally:
         dist.barrier()

@@ -198,6 +198,22 @@ const char* gmm_sm100_moe_last_error(void);
  * reference kernel has no device-side error path). */
 int gmm_sm100_device_error(int* status_out, int clear);
 
+/* Test hook of the bounded-wait path; no reference counterpart (the
+ * reference kernel has no device-side timeout).  Runs gmm_sm100_forward
+ * (bf16 / fp16, no workspace; the 128-row or CTA-pair kernel, per the tile
+ * kind in force) with two changes: every pipeline wait gives up after wait_s
+ * seconds (0 < wait_s <= 2) instead of 2 s, and the TMA producer of the first
+ * tile of CTA (pair) 0 skips the loads of k-block drop_k_block.  The MMA
+ * warp's wait for that stage then runs out, the CTA drains the copies it has
+ * in flight, frees its tensor memory and returns, and the device error word
+ * reads GMM_ERR_DEVICE_TIMEOUT (gmm_sm100_device_error).  D is left partly
+ * unwritten.  Nothing faults or hangs: the failure is the one the bounded
+ * waits exist for, made on purpose. */
+int gmm_sm100_forward_inject_timeout(const void* A, const void* B, const int64_t* batch_sizes,
+                                     int64_t num_experts, int64_t num_tokens, int64_t dim,
+                                     int64_t dim_out, int dtype, int trans_b, void* D,
+                                     int drop_k_block, double wait_s, void* stream);
+
 /* ---------------------------------------------------------------- expert parallelism
  * No reference counterpart (the reference runs on one GPU).  A rank owning
  * num_local_experts experts receives, for local expert e, world segments of
@@ -214,6 +230,20 @@ int gmm_sm100_device_error(int* status_out, int clear);
 int gmm_sm100_ep_gather(void* X, const void* const* src_peers, const int64_t* counts,
                         const int64_t* src_rows, int64_t num_local_experts, int world,
                         int rank_base, int64_t row_bytes, void* stream);
+
+/* Cross-rank barrier of the layer, over peer memory (one small kernel; no
+ * NCCL call).  flag_peers[s] points at rank s's `world` int32 flag slots (a
+ * symmetric-memory buffer, zeroed before first use); every rank calls it
+ * with the same, growing epoch.  Each rank posts epoch into every peer's slot
+ * with release semantics at system scope -- so all the writes this rank
+ * enqueued on `stream` before the barrier (its token rows, its peer stores)
+ * are visible to the peers -- and waits for every peer's post with acquire.
+ * The wait is bounded by timeout_s: past it the kernel records
+ * GMM_ERR_DEVICE_TIMEOUT in the device error word (gmm_sm100_device_error)
+ * and returns, so a rank that never arrives is reported instead of hanging
+ * the GPU. */
+int gmm_sm100_ep_barrier(int* const* flag_peers, int world, int rank, int epoch, double timeout_s,
+                         void* stream);
 
 /* Local grouped GEMM with the combine fused into its epilogue: the result of
  * row i of segment j of local expert e goes straight to row
