@@ -292,7 +292,7 @@ def _config_entry(W, cid, dev, steps, warmup, peaks):
                           "peak": peaks["hbm_gbs"] if hbm_bound else peaks["bf16_tflops"],
                           "unit": "GB/s" if hbm_bound else "TFLOP/s"},
              "l2": W.l2_note(cfg, bs), "steps": steps, "parity": par,
-             "kernel_launches_per_step": 2 if cfg.dtype == torch.float32 else 1}
+             "kernel_launches_per_step": 1}
     del a, b, out, flush
     torch.cuda.empty_cache()
     return entry
@@ -320,7 +320,7 @@ def run_single(args):
         a, b = W.make_inputs(cfg, "cuda")
     flops = cfg.flops()
     alg_bytes = cfg.algorithmic_bytes(bs)
-    launches_per_step = 2 if cfg.dtype == torch.float32 else 1  # fp32: split pre-pass + GEMM
+    launches_per_step = 1  # one persistent kernel (fp32 included: TF32 split in shared memory)
 
     def step():
         return hopper_gmm_fwd(a, b, bs, cfg.trans_b)

@@ -124,12 +124,13 @@ struct Cfg {
   static constexpr int kABytes = BM * BK * kElem;
   static constexpr int kBBytes = BN * BK * kElem;
   static constexpr int kStageBytes = kParts * (kABytes + kBBytes);
+  static constexpr int kLoadBytes = kABytes + kBBytes;  // bytes TMA brings in per stage
+  static constexpr int kPanelCols = 128 / kElem;        // MN-major B: columns per 128-byte panel
   static constexpr int kTmemCols = 2 * BN;  // double-buffered fp32 accumulator
   static constexpr uint32_t kIdesc =
       make_idesc(kTf32 ? 2u : (kKind == kKindBf16 ? 1u : 0u), kBMnMajor, BM, BN);
   static constexpr int kBarBytes = 256;
   static constexpr int kSmemBytes = kStages * kStageBytes + kBarBytes + kEpiStageBytes + kDevTableBytes + 1024;
-  static_assert(!(kTf32 && kBMnMajor), "fp32 B is staged K-major by the split pre-pass");
   static_assert(kABytes % 1024 == 0 && kBBytes % 1024 == 0, "swizzle atoms need 1 KB alignment");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
@@ -442,6 +443,19 @@ __device__ __forceinline__ void drain_slab_swiglu(const GmmParams& p, const Tabl
   }
 }
 
+// Splits x into a TF32-exact high part (low 13 mantissa bits cleared) and the
+// fp32 remainder, so that three TF32 products hi*hi + hi*lo + lo*hi recover
+// close to fp32 accuracy.  Non-finite values pass through in hi with lo = 0.
+__device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
+  if (isfinite(x)) {
+    hi = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+    lo = x - hi;
+  } else {
+    hi = x;
+    lo = 0.0f;
+  }
+}
+
 template <int kKind, bool kBMnMajor>
 __global__ void __launch_bounds__(kThreads, 1) gmm_persistent_kernel(const __grid_constant__ GmmParams p) {
   using C = Cfg<kKind, kBMnMajor>;
@@ -457,14 +471,17 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_persistent_kernel(const __gri
   uint64_t* tfull_bar = bars + 2 * C::kStages;     // MMA -> epilogue (2 accumulators)
   uint64_t* tempty_bar = bars + 2 * C::kStages + 2;  // epilogue -> MMA
   uint64_t* drain_bar = bars + 2 * C::kStages + 4;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * C::kStages + 5);
+  uint64_t* conv_bar = bars + 2 * C::kStages + 5;  // fp32: hi/lo split done -> MMA
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * C::kStages + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   uint8_t* epi_stage = smem + C::kStages * C::kStageBytes + C::kBarBytes;
+  static_assert((3 * C::kStages + 6) * 8 <= C::kBarBytes, "barrier area");
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(smem_u32(full_bar + s), 1);
       mbar_init(smem_u32(empty_bar + s), 1);
+      mbar_init(smem_u32(conv_bar + s), 2);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(smem_u32(tfull_bar + a), 1);
@@ -477,10 +494,6 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_persistent_kernel(const __gri
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&p.tmap_a);
     prefetch_tmap(&p.tmap_b);
-    if (C::kTf32) {
-      prefetch_tmap(&p.tmap_a2);
-      prefetch_tmap(&p.tmap_b2);
-    }
   }
   if (warp == 2) {
     tmem_alloc(smem_u32(tmem_slot), C::kTmemCols);
@@ -531,15 +544,20 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_persistent_kernel(const __gri
             continue;
           }
           const uint32_t fb = smem_u32(full_bar + stage);
-          mbar_arrive_expect_tx(fb, C::kStageBytes);
+          mbar_arrive_expect_tx(fb, C::kLoadBytes);
           uint8_t* sa = smem + stage * C::kStageBytes;
           uint8_t* sb = sa + C::kParts * C::kABytes;
           const int k0 = kb * C::BK;
           tma_load_2d(smem_u32(sa), &p.tmap_a, fb, k0, t.row0);
-          if (C::kTf32) {
-            tma_load_2d(smem_u32(sa + C::kABytes), &p.tmap_a2, fb, k0, t.row0);
-            tma_load_3d(smem_u32(sb), &p.tmap_b, fb, k0, t.n0, t.expert);
-            tma_load_3d(smem_u32(sb + C::kBBytes), &p.tmap_b2, fb, k0, t.n0, t.expert);
+          if (C::kTf32) {  // raw fp32 tiles; the converter warps split them in place
+            if (kBMnMajor) {
+#pragma unroll
+              for (int c = 0; c < C::BN / C::kPanelCols; ++c)
+                tma_load_3d(smem_u32(sb + c * (C::BK * 128)), &p.tmap_b, fb, t.n0 + C::kPanelCols * c, k0,
+                            t.expert);
+            } else {
+              tma_load_3d(smem_u32(sb), &p.tmap_b, fb, k0, t.n0, t.expert);
+            }
           } else if (kBMnMajor) {
             // B[e] is [K, N] (N contiguous): BN/64 panels of [BK rows][64 cols];
             // SwiGLU tiles take two gate panels and the two matching up panels.
@@ -582,7 +600,7 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_persistent_kernel(const __gri
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * C::BN;
         for (int kb = 0; kb < k_blocks; ++kb) {
-          if (!mbar_wait(smem_u32(full_bar + stage), phase, abort_flag, wait_ns)) {
+          if (!mbar_wait(smem_u32((C::kTf32 ? conv_bar : full_bar) + stage), phase, abort_flag, wait_ns)) {
             ok = false;
             break;
           }
@@ -594,13 +612,17 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_persistent_kernel(const __gri
             const uint32_t acc_flag = (kb | ks) != 0 ? 1u : 0u;
             const uint64_t adesc = make_sw128_desc(sa + ks * 32, 16, 1024);
             uint64_t bdesc;
-            if (kBMnMajor)
+            if (kBMnMajor && C::kTf32)  // MN-major tf32: 32-byte-atom swizzle
+              bdesc = make_sw128_atom32_desc(sb + ks * C::kUmmaK * 128, C::BK * 128, 512);
+            else if (kBMnMajor)
               bdesc = make_sw128_desc(sb + ks * C::kUmmaK * 128, C::BK * 128, 1024);
             else
               bdesc = make_sw128_desc(sb + ks * 32, 16, 1024);
             if (C::kTf32) {
               const uint64_t adesc_lo = make_sw128_desc(sa + C::kABytes + ks * 32, 16, 1024);
-              const uint64_t bdesc_lo = make_sw128_desc(sb + C::kBBytes + ks * 32, 16, 1024);
+              const uint64_t bdesc_lo =
+                  kBMnMajor ? make_sw128_atom32_desc(sb + C::kBBytes + ks * C::kUmmaK * 128, C::BK * 128, 512)
+                            : make_sw128_desc(sb + C::kBBytes + ks * 32, 16, 1024);
               mma_tf32_ss(d_tmem, adesc, bdesc, C::kIdesc, acc_flag);    // hi * hi
               mma_tf32_ss(d_tmem, adesc, bdesc_lo, C::kIdesc, 1u);      // hi * lo
               mma_tf32_ss(d_tmem, adesc_lo, bdesc, C::kIdesc, 1u);      // lo * hi
@@ -620,6 +642,50 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_persistent_kernel(const __gri
       // Retire every MMA this thread issued before TMEM can be released.
       mma_commit(smem_u32(drain_bar));
       mbar_wait_drain(smem_u32(drain_bar), 0);
+    }
+  } else if (C::kTf32 && (warp == 2 || warp == 3)) {
+    // ------------------------------------------------------------ fp32 split (converter)
+    // Each landed fp32 stage is split in shared memory: x -> hi (low 13
+    // mantissa bits cleared, exact in TF32) in place, x - hi -> the stage's lo
+    // copy at the same offset.  The split is element-wise, so the swizzled
+    // layout is preserved; the writes are fenced into the async proxy before
+    // the MMA warp (which waits on conv_bar) hands them to the tensor cores.
+    const int ct = threadIdx.x - 64;  // 0..63
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
+      for (int kb = 0; kb < k_blocks; ++kb) {
+        if (!mbar_wait(smem_u32(full_bar + stage), phase, abort_flag, wait_ns)) {
+          ok = false;
+          break;
+        }
+        const uint32_t base = smem_u32(smem + stage * C::kStageBytes);
+        constexpr int kChunksA = C::kABytes / 16, kChunks = (C::kABytes + C::kBBytes) / 16;
+#pragma unroll 4
+        for (int i = ct; i < kChunks; i += 64) {
+          // A: x at [0, kABytes), lo at [kABytes, 2 kABytes); B: x at 2 kABytes, lo kBBytes further
+          const uint32_t off = i < kChunksA ? i * 16 : 2 * C::kABytes + (i - kChunksA) * 16;
+          const uint32_t lo_off = off + (i < kChunksA ? C::kABytes : C::kBBytes);
+          const uint4 v = ld_shared_v4(base + off);
+          float h0, h1, h2, h3, l0, l1, l2, l3;
+          split_tf32(__uint_as_float(v.x), h0, l0);
+          split_tf32(__uint_as_float(v.y), h1, l1);
+          split_tf32(__uint_as_float(v.z), h2, l2);
+          split_tf32(__uint_as_float(v.w), h3, l3);
+          st_shared_v4(base + off, make_uint4(__float_as_uint(h0), __float_as_uint(h1), __float_as_uint(h2),
+                                              __float_as_uint(h3)));
+          st_shared_v4(base + lo_off, make_uint4(__float_as_uint(l0), __float_as_uint(l1), __float_as_uint(l2),
+                                                 __float_as_uint(l3)));
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(conv_bar + stage));
+        if (++stage == C::kStages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ epilogue
@@ -664,90 +730,6 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_persistent_kernel(const __gri
     tmem_dealloc(tmem_base, C::kTmemCols);
   }
   if (threadIdx.x == 0 && *abort_flag) atomicCAS(&g_device_error, 0, GMM_ERR_DEVICE_TIMEOUT);
-}
-
-// ------------------------------------------------------------------ fp32 pre-pass
-// Splits x into a TF32-exact high part (low 13 mantissa bits cleared) and the
-// fp32 remainder, so that three TF32 products hi*hi + hi*lo + lo*hi recover
-// close to fp32 accuracy.  Non-finite values pass through in hi with lo = 0.
-__device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
-  if (isfinite(x)) {
-    hi = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
-    lo = x - hi;
-  } else {
-    hi = x;
-    lo = 0.0f;
-  }
-}
-
-__device__ __forceinline__ void split_tf32_vec(const float4* __restrict__ x, float4* __restrict__ hi,
-                                               float4* __restrict__ lo, long long i) {
-  const float4 v = x[i];
-  float4 h, l;
-  split_tf32(v.x, h.x, l.x);
-  split_tf32(v.y, h.y, l.y);
-  split_tf32(v.z, h.z, l.z);
-  split_tf32(v.w, h.w, l.w);
-  hi[i] = h;
-  lo[i] = l;
-}
-
-struct SplitArgs {
-  const float4* a;
-  float4* a_hi;
-  float4* a_lo;
-  long long n4a;  // float4s of A
-  int a_blocks;   // blocks [0, a_blocks) split A; the rest split B
-  const float* b;
-  float* b_hi;
-  float* b_lo;
-  long long n4b;  // float4s of B (trans_b)
-  int K, N, trans_b;
-  int nt_n, nt_k;       // 32x32 tiles of one B[e] (transposing split)
-  long long b_tiles;    // E * nt_n * nt_k
-};
-
-// The whole fp32 pre-pass in one launch: A (and a K-major B) split element by
-// element; a [K, N] B split while transposed to [N, K] (K contiguous) through
-// 32x32 shared-memory tiles, for the K-major TF32 operands of the GEMM.
-__global__ void __launch_bounds__(256) split_operands_kernel(const SplitArgs sa) {
-  if (static_cast<int>(blockIdx.x) < sa.a_blocks) {
-    for (long long i = blockIdx.x * 256LL + threadIdx.x; i < sa.n4a; i += sa.a_blocks * 256LL)
-      split_tf32_vec(sa.a, sa.a_hi, sa.a_lo, i);
-    return;
-  }
-  const long long bb = blockIdx.x - sa.a_blocks, nb = gridDim.x - sa.a_blocks;
-  if (sa.trans_b) {
-    const float4* b4 = reinterpret_cast<const float4*>(sa.b);
-    for (long long i = bb * 256 + threadIdx.x; i < sa.n4b; i += nb * 256)
-      split_tf32_vec(b4, reinterpret_cast<float4*>(sa.b_hi), reinterpret_cast<float4*>(sa.b_lo), i);
-    return;
-  }
-  __shared__ float tile[32][33];
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8 threads
-  const long long per_e = static_cast<long long>(sa.nt_n) * sa.nt_k;
-  for (long long t = bb; t < sa.b_tiles; t += nb) {
-    const long long e = t / per_e;
-    const int r = static_cast<int>(t - e * per_e);
-    const int k0 = (r / sa.nt_n) * 32, n0 = (r % sa.nt_n) * 32;
-    const long long e_off = e * sa.K * sa.N;
-    for (int i = ty; i < 32; i += 8) {
-      const int k = k0 + i, n = n0 + tx;
-      tile[i][tx] = (k < sa.K && n < sa.N) ? sa.b[e_off + static_cast<long long>(k) * sa.N + n] : 0.f;
-    }
-    __syncthreads();
-    for (int i = ty; i < 32; i += 8) {
-      const int n = n0 + i, k = k0 + tx;
-      if (n < sa.N && k < sa.K) {
-        float h, l;
-        split_tf32(tile[tx][i], h, l);
-        const long long o = e_off + static_cast<long long>(n) * sa.K + k;
-        sa.b_hi[o] = h;
-        sa.b_lo[o] = l;
-      }
-    }
-    __syncthreads();
-  }
 }
 
 // ------------------------------------------------------------ expert-parallel dispatch
@@ -903,8 +885,6 @@ struct Plan {
   int n_tiles = 0, k_blocks = 0, total_tiles = 0;
   std::vector<int32_t> table;
   size_t table_bytes = 0;    // device table bytes (0 when inline)
-  size_t split_bytes = 0;    // fp32 hi/lo staging
-  size_t a_part = 0, b_part = 0;
 };
 
 int elem_size(int dtype) { return dtype == GMM_DTYPE_F32 ? 4 : 2; }
@@ -957,21 +937,17 @@ int make_plan(const int64_t* bs, int64_t E, int64_t T, int64_t K, int64_t N, int
   row_off[groups] = static_cast<int32_t>(row);
   tile_off[groups] = static_cast<int32_t>(tiles);
   pl.table_bytes = groups > kInlineGroups ? round_up(pl.table.size() * sizeof(int32_t), 256) : 0;
-  if (dtype == GMM_DTYPE_F32) {
-    pl.a_part = round_up(static_cast<size_t>(T) * K * 4, 256);
-    pl.b_part = round_up(static_cast<size_t>(E) * K * N * 4, 256);
-    pl.split_bytes = 2 * pl.a_part + 2 * pl.b_part;
-  }
   return GMM_OK;
 }
 
 int encode(CUtensorMap* m, CUtensorMapDataType type, int rank, const void* ptr,
-           const cuuint64_t* dims, const cuuint64_t* strides_bytes, const cuuint32_t* box) {
+           const cuuint64_t* dims, const cuuint64_t* strides_bytes, const cuuint32_t* box,
+           CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   auto fn = encode_tiled();
   if (!fn) return fail(GMM_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
   cuuint32_t estr[5] = {1, 1, 1, 1, 1};
   CUresult r = fn(m, type, rank, const_cast<void*>(ptr), dims, strides_bytes, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(GMM_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
   return GMM_OK;
@@ -1122,62 +1098,28 @@ bool append_ep_table(Plan& pl, const int64_t* local_bs, int64_t E, const EpRoute
   return true;
 }
 
-// The fp32 pre-pass (one launch): hi/lo splits of A into a_hi/a_lo and of B,
-// K-major, into b_hi/b_lo.
-int launch_split(const void* A, const void* B, float* a_hi, float* a_lo, float* b_hi, float* b_lo, int64_t T,
-                 int64_t K, int64_t N, int64_t E, int trans_b, int sm_count, cudaStream_t stream) {
-  SplitArgs sa;
-  sa.a = reinterpret_cast<const float4*>(A);
-  sa.a_hi = reinterpret_cast<float4*>(a_hi);
-  sa.a_lo = reinterpret_cast<float4*>(a_lo);
-  sa.n4a = T * K / 4;
-  sa.a_blocks = static_cast<int>(std::max<long long>(1, std::min<long long>((sa.n4a + 255) / 256, 4LL * sm_count)));
-  sa.b = static_cast<const float*>(B);
-  sa.b_hi = b_hi;
-  sa.b_lo = b_lo;
-  sa.n4b = E * K * N / 4;
-  sa.K = static_cast<int>(K);
-  sa.N = static_cast<int>(N);
-  sa.trans_b = trans_b ? 1 : 0;
-  sa.nt_n = static_cast<int>((N + 31) / 32);
-  sa.nt_k = static_cast<int>((K + 31) / 32);
-  sa.b_tiles = E * sa.nt_n * static_cast<long long>(sa.nt_k);
-  const long long b_blocks = std::max<long long>(
-      1, trans_b ? std::min<long long>((sa.n4b + 255) / 256, 4LL * sm_count)
-                 : std::min<long long>(sa.b_tiles, 16LL * sm_count));
-  split_operands_kernel<<<static_cast<unsigned>(sa.a_blocks + b_blocks), 256, 0, stream>>>(sa);
-  cudaError_t ce = cudaGetLastError();
-  return ce == cudaSuccess ? GMM_OK : cuda_fail(ce, "split pre-pass launch");
-}
-
-// Operand preparation (fp32 hi/lo split pre-pass, tensor maps) and the
-// launch of the chosen kernel variant.  `grid_tiles` caps the grid (the tile
-// count when the host knows it).
-int setup_and_launch(GmmParams& prm, const void* A, const void* B, uint8_t* ws, size_t a_part,
-                     size_t b_part, int64_t T, int64_t K, int64_t N, int64_t E, int dtype, int trans_b,
-                     int64_t tile_rows, int act, int grid_tiles, DeviceInfo* di, cudaStream_t stream,
-                     bool swap = false) {
+// Tensor maps and the launch of the chosen kernel variant.  `grid_tiles`
+// caps the grid (the tile count when the host knows it).
+int setup_and_launch(GmmParams& prm, const void* A, const void* B, int64_t T, int64_t K, int64_t N, int64_t E,
+                     int dtype, int trans_b, int64_t tile_rows, int act, int grid_tiles, DeviceInfo* di,
+                     cudaStream_t stream, bool swap = false) {
   int rc = GMM_OK;
-  struct {
-    size_t a_part, b_part, split_bytes;
-    int total_tiles;
-  } pl{a_part, b_part, 2 * a_part + 2 * b_part, grid_tiles};
   const cuuint64_t uT = T, uK = K, uN = N, uE = E;
-  if (dtype == GMM_DTYPE_F32) {
-    float* a_hi = reinterpret_cast<float*>(ws);
-    float* a_lo = reinterpret_cast<float*>(ws + pl.a_part);
-    float* b_hi = reinterpret_cast<float*>(ws + 2 * pl.a_part);
-    float* b_lo = reinterpret_cast<float*>(ws + 2 * pl.a_part + pl.b_part);
-    if ((rc = launch_split(A, B, a_hi, a_lo, b_hi, b_lo, T, K, N, E, trans_b, di->sm_count, stream))) return rc;
+  if (dtype == GMM_DTYPE_F32) {  // raw fp32 operands; the kernel splits them into TF32 hi/lo in shared memory
     const cuuint64_t adims[2] = {uK, uT}, astr[1] = {uK * 4};
     const cuuint32_t abox[2] = {32, 128};
-    const cuuint64_t bdims[3] = {uK, uN, uE}, bstr[2] = {uK * 4, uN * uK * 4};
-    const cuuint32_t bbox[3] = {32, 128, 1};
-    if ((rc = encode(&prm.tmap_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a_hi, adims, astr, abox)) ||
-        (rc = encode(&prm.tmap_a2, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a_lo, adims, astr, abox)) ||
-        (rc = encode(&prm.tmap_b, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, b_hi, bdims, bstr, bbox)) ||
-        (rc = encode(&prm.tmap_b2, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, b_lo, bdims, bstr, bbox)))
-      return rc;
+    if ((rc = encode(&prm.tmap_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, A, adims, astr, abox))) return rc;
+    if (trans_b) {  // B[e] is [N, K], K contiguous
+      const cuuint64_t bdims[3] = {uK, uN, uE}, bstr[2] = {uK * 4, uN * uK * 4};
+      const cuuint32_t bbox[3] = {32, 128, 1};
+      if ((rc = encode(&prm.tmap_b, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, B, bdims, bstr, bbox))) return rc;
+    } else {  // B[e] is [K, N], N contiguous: [32 k][32 cols] panels, 32-byte-atom swizzle (MN-major tf32)
+      const cuuint64_t bdims[3] = {uN, uK, uE}, bstr[2] = {uN * 4, uK * uN * 4};
+      const cuuint32_t bbox[3] = {32, 32, 1};
+      if ((rc = encode(&prm.tmap_b, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, B, bdims, bstr, bbox,
+                       CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B)))
+        return rc;
+    }
   } else {
     const CUtensorMapDataType tt =
         dtype == GMM_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -1199,8 +1141,10 @@ int setup_and_launch(GmmParams& prm, const void* A, const void* B, uint8_t* ws, 
     }
   }
 
-  const int grid = std::max(1, std::min(pl.total_tiles, di->sm_count));
-  if (dtype == GMM_DTYPE_F32) return launch_variant<kKindTf32x3, false>(prm, grid, stream, di, 0);
+  const int grid = std::max(1, std::min(grid_tiles, di->sm_count));
+  if (dtype == GMM_DTYPE_F32)
+    return trans_b ? launch_variant<kKindTf32x3, false>(prm, grid, stream, di, 0)
+                   : launch_variant<kKindTf32x3, true>(prm, grid, stream, di, 15);
   if (swap) {
     if (dtype == GMM_DTYPE_BF16)
       return trans_b ? launch_swap<kKindBf16, false>(prm, grid, stream, di, 11)
@@ -1210,10 +1154,10 @@ int setup_and_launch(GmmParams& prm, const void* A, const void* B, uint8_t* ws, 
   }
   if (tile_rows == 256) {
     if (dtype == GMM_DTYPE_BF16)
-      return trans_b ? launch_pair<kKindBf16, false>(prm, pl.total_tiles, stream, di, 5)
-                     : launch_pair<kKindBf16, true>(prm, pl.total_tiles, stream, di, 6);
-    return trans_b ? launch_pair<kKindF16, false>(prm, pl.total_tiles, stream, di, 7)
-                   : launch_pair<kKindF16, true>(prm, pl.total_tiles, stream, di, 8);
+      return trans_b ? launch_pair<kKindBf16, false>(prm, grid_tiles, stream, di, 5)
+                     : launch_pair<kKindBf16, true>(prm, grid_tiles, stream, di, 6);
+    return trans_b ? launch_pair<kKindF16, false>(prm, grid_tiles, stream, di, 7)
+                   : launch_pair<kKindF16, true>(prm, grid_tiles, stream, di, 8);
   }
   if (dtype == GMM_DTYPE_BF16)
     return trans_b ? launch_variant<kKindBf16, false>(prm, grid, stream, di, 1)
@@ -1304,7 +1248,7 @@ int launch_impl(const PlanObj& po, const Plan& pl, const void* A, const void* B,
   if ((K * es) % 16 != 0)
     return fail(GMM_ERR_ALIGNMENT, "dim * element size must be a multiple of 16 bytes, got dim=" +
                                        std::to_string(K));
-  const size_t need = pl.split_bytes + pl.table_bytes;
+  const size_t need = pl.table_bytes;
   if (need > 0 && (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255u)))
     return fail(GMM_ERR_WORKSPACE, "workspace needs " + std::to_string(need) + " bytes (256-byte aligned), got " +
                                        std::to_string(workspace_bytes));
@@ -1332,19 +1276,18 @@ int launch_impl(const PlanObj& po, const Plan& pl, const void* A, const void* B,
     prm.ep_rank_base = ((ep->rank_base % ep->world) + ep->world) % ep->world;
     for (int s = 0; s < ep->world; ++s) prm.d_peer[s] = ep->out_peers[s];
   }
-  uint8_t* ws = static_cast<uint8_t*>(workspace);
   if (pl.table_bytes == 0) {
     std::memcpy(prm.inline_table, pl.table.data(), pl.table.size() * sizeof(int32_t));
     prm.ext_table = nullptr;
   } else {
-    uint8_t* tdev = ws + pl.split_bytes;
-    ce = cudaMemcpyAsync(tdev, pl.table.data(), pl.table.size() * sizeof(int32_t), cudaMemcpyHostToDevice, stream);
+    ce = cudaMemcpyAsync(workspace, pl.table.data(), pl.table.size() * sizeof(int32_t), cudaMemcpyHostToDevice,
+                         stream);
     if (ce != cudaSuccess) return cuda_fail(ce, "cudaMemcpyAsync(table)");
-    prm.ext_table = reinterpret_cast<const int32_t*>(tdev);
+    prm.ext_table = static_cast<const int32_t*>(workspace);
   }
 
-  return setup_and_launch(prm, A, B, ws, pl.a_part, pl.b_part, T, K, N, E, dtype, trans_b, tile_rows, act,
-                          pl.total_tiles, di, stream, kind == kTileSwap);
+  return setup_and_launch(prm, A, B, T, K, N, E, dtype, trans_b, tile_rows, act, pl.total_tiles, di, stream,
+                          kind == kTileSwap);
 }
 
 int forward_impl(const void* A, const void* B, const int64_t* batch_sizes, int64_t num_experts,
@@ -1404,7 +1347,7 @@ size_t gmm_sm100_workspace_size(const int64_t* batch_sizes, int64_t num_experts,
   (void)trans_b;
   Plan pl;
   if (make_plan(batch_sizes, num_experts, num_tokens, dim, dim_out, dtype, pl) != GMM_OK) return 0;
-  return pl.split_bytes + pl.table_bytes;
+  return pl.table_bytes;
 }
 
 int gmm_sm100_forward(const void* A, const void* B, const int64_t* batch_sizes, int64_t num_experts,
@@ -1430,7 +1373,7 @@ int gmm_sm100_plan(const int64_t* batch_sizes, int64_t num_experts, int64_t num_
 }
 
 size_t gmm_sm100_plan_workspace_size(const gmm_sm100_plan_t* plan) {
-  return plan ? plan->po.pl.split_bytes + plan->po.pl.table_bytes : 0;
+  return plan ? plan->po.pl.table_bytes : 0;
 }
 
 int gmm_sm100_launch(const gmm_sm100_plan_t* plan, const void* A, const void* B, void* D, void* workspace,
@@ -1452,7 +1395,7 @@ size_t gmm_sm100_ep_workspace_size(const int64_t* counts, int64_t num_local_expe
   if (make_plan(local_bs.data(), num_local_experts, num_rows, dim, dim_out, dtype, pl) != GMM_OK) return 0;
   EpRoute route{world, nullptr, counts, zeros.data(), 0};
   if (!append_ep_table(pl, local_bs.data(), num_local_experts, route)) return 0;
-  return pl.split_bytes + pl.table_bytes;
+  return pl.table_bytes;
 }
 
 int gmm_sm100_forward_ep(const void* X, const void* B, const int64_t* counts, const int64_t* dst_rows,
@@ -1554,9 +1497,8 @@ int gmm_sm100_forward_swiglu(const void* A, const void* B, const int64_t* batch_
 
 size_t gmm_sm100_dev_workspace_size(int64_t num_experts, int64_t rows_cap, int64_t dim, int64_t dim_out,
                                     int dtype) {
-  if (dtype != GMM_DTYPE_F32 || num_experts <= 0 || rows_cap <= 0) return 0;
-  return 2 * round_up(static_cast<size_t>(rows_cap) * dim * 4, 256) +
-         2 * round_up(static_cast<size_t>(num_experts) * dim * dim_out * 4, 256);
+  (void)num_experts, (void)rows_cap, (void)dim, (void)dim_out, (void)dtype;
+  return 0;  // the kernels build their tables in shared memory and split fp32 in shared memory
 }
 
 int gmm_sm100_forward_dev(const void* A, const void* B, const int32_t* batch_sizes_dev, int64_t num_experts,
@@ -1592,9 +1534,7 @@ int gmm_sm100_forward_dev(const void* A, const void* B, const int32_t* batch_siz
   if (!A || !B || !aligned16(A) || !aligned16(B))
     return fail(GMM_ERR_ALIGNMENT, "A and B must be non-null and 16-byte aligned");
   if ((K * es) % 16 != 0) return fail(GMM_ERR_ALIGNMENT, "dim * element size must be a multiple of 16 bytes");
-  const size_t need = gmm_sm100_dev_workspace_size(E, T, K, N, dtype);
-  if (need > 0 && (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255u)))
-    return fail(GMM_ERR_WORKSPACE, "workspace needs " + std::to_string(need) + " bytes (256-byte aligned)");
+  (void)workspace, (void)workspace_bytes;  // none needed (gmm_sm100_dev_workspace_size is 0)
   // Tile kind from the capacity alone (the sizes are only known on the device):
   // CTA pairs when the capacity averages at least 384 rows per expert,
   // swap-AB tiles when it averages at most 16 (decode), else 128-row tiles.
@@ -1624,10 +1564,7 @@ int gmm_sm100_forward_dev(const void* A, const void* B, const int32_t* batch_siz
   prm.dev_experts = static_cast<int>(E);
   prm.rows_cap = static_cast<int>(T);
   prm.tile_rows = static_cast<int>(tile_rows);
-  const size_t a_part = dtype == GMM_DTYPE_F32 ? round_up(static_cast<size_t>(T) * K * 4, 256) : 0;
-  const size_t b_part = dtype == GMM_DTYPE_F32 ? round_up(static_cast<size_t>(E) * K * N * 4, 256) : 0;
-  return setup_and_launch(prm, A, B, static_cast<uint8_t*>(workspace), a_part, b_part, T, K, N, E, dtype,
-                          trans_b, tile_rows, prm.act, INT32_MAX, di, stream, swap);
+  return setup_and_launch(prm, A, B, T, K, N, E, dtype, trans_b, tile_rows, prm.act, INT32_MAX, di, stream, swap);
 }
 
 int gmm_sm100_forward_vark(const void* A, const void* B, const int64_t* batch_sizes, int64_t num_experts,
@@ -1788,7 +1725,9 @@ extern "C" int gmm_sm100_forward_f32_noalloc(const float* A, const float* B,
   if (!aligned16(D)) return fail(GMM_ERR_ALIGNMENT, "D must be 16-byte aligned");
   if ((N * 4) % 16 != 0)
     return fail(GMM_ERR_ALIGNMENT, "dim_out must be a multiple of 4 for fp32, got " + std::to_string(N));
-  const size_t need = pl.split_bytes + pl.table_bytes;
+  // The only scratch of the fp32 path is the tile table of more than 1024
+  // non-empty experts (the TF32 split happens in shared memory).
+  const size_t need = pl.table_bytes;
   if (need > GMM_SM100_NOALLOC_SCRATCH_BYTES)
     return fail(GMM_ERR_TOO_LARGE, "gmm_sm100_forward_f32_noalloc needs " + std::to_string(need) +
                                        " bytes of scratch; its fixed scratch holds " +
@@ -1807,9 +1746,6 @@ extern "C" int gmm_sm100_forward_f32_noalloc(const float* A, const float* B,
   if (!aligned16(A) || !aligned16(B)) return fail(GMM_ERR_ALIGNMENT, "A and B must be 16-byte aligned");
   if ((K * 4) % 16 != 0)
     return fail(GMM_ERR_ALIGNMENT, "dim must be a multiple of 4 for fp32, got " + std::to_string(K));
-  void* scratch = nullptr;
-  if ((rc = noalloc_scratch_address(dev, &scratch)) != GMM_OK) return rc;
-  uint8_t* ws = static_cast<uint8_t*>(scratch);
 
   GmmParams prm;
   std::memset(&prm, 0, sizeof(prm));
@@ -1820,30 +1756,17 @@ extern "C" int gmm_sm100_forward_f32_noalloc(const float* A, const float* B,
   prm.k_blocks = pl.k_blocks;
   prm.total_tiles = pl.total_tiles;
   prm.dim_out = static_cast<int>(N);
+  prm.tile_rows = 128;
   if (pl.table_bytes == 0) {
     std::memcpy(prm.inline_table, pl.table.data(), pl.table.size() * sizeof(int32_t));
   } else {
-    uint8_t* tdev = ws + pl.split_bytes;
-    ce = cudaMemcpyAsync(tdev, pl.table.data(), pl.table.size() * sizeof(int32_t), cudaMemcpyHostToDevice, stream);
+    // The table is written in full (stream-ordered) before the kernel reads it.
+    void* scratch = nullptr;
+    if ((rc = noalloc_scratch_address(dev, &scratch)) != GMM_OK) return rc;
+    ce = cudaMemcpyAsync(scratch, pl.table.data(), pl.table.size() * sizeof(int32_t), cudaMemcpyHostToDevice,
+                         stream);
     if (ce != cudaSuccess) return cuda_fail(ce, "cudaMemcpyAsync(table)");
-    prm.ext_table = reinterpret_cast<const int32_t*>(tdev);
+    prm.ext_table = static_cast<const int32_t*>(scratch);
   }
-  // Every byte of the scratch that the GEMM reads is rewritten below first.
-  float* a_hi = reinterpret_cast<float*>(ws);
-  float* a_lo = reinterpret_cast<float*>(ws + pl.a_part);
-  float* b_hi = reinterpret_cast<float*>(ws + 2 * pl.a_part);
-  float* b_lo = reinterpret_cast<float*>(ws + 2 * pl.a_part + pl.b_part);
-  if ((rc = launch_split(A, B, a_hi, a_lo, b_hi, b_lo, T, K, N, E, trans_b, di->sm_count, stream))) return rc;
-  const cuuint64_t uT = T, uK = K, uN = N, uE = E;
-  const cuuint64_t adims[2] = {uK, uT}, astr[1] = {uK * 4};
-  const cuuint32_t abox[2] = {32, 128};
-  const cuuint64_t bdims[3] = {uK, uN, uE}, bstr[2] = {uK * 4, uN * uK * 4};
-  const cuuint32_t bbox[3] = {32, 128, 1};
-  if ((rc = encode(&prm.tmap_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a_hi, adims, astr, abox)) ||
-      (rc = encode(&prm.tmap_a2, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a_lo, adims, astr, abox)) ||
-      (rc = encode(&prm.tmap_b, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, b_hi, bdims, bstr, bbox)) ||
-      (rc = encode(&prm.tmap_b2, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, b_lo, bdims, bstr, bbox)))
-    return rc;
-  const int grid = std::max(1, std::min(pl.total_tiles, di->sm_count));
-  return launch_variant<kKindTf32x3, false>(prm, grid, stream, di, 0);
+  return setup_and_launch(prm, A, B, T, K, N, E, GMM_DTYPE_F32, trans_b, 128, 0, pl.total_tiles, di, stream);
 }

@@ -218,6 +218,23 @@ __device__ __forceinline__ uint64_t make_sw128_desc(uint32_t smem_addr, uint32_t
   return d;
 }
 
+// The same descriptor for an MN-major 32-bit (tf32) operand, which needs the
+// "128-byte swizzle, 32-byte atom" layout (layout type 1): 128-byte rows whose
+// four 32-byte chunks are permuted by (row % 4), written by TMA with
+// CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B.  The swizzle pattern spans 4 rows
+// (512 B), so sbo = 512 B for rows 128 B apart; lbo = stride between 32-column
+// (128-byte) panels.
+__device__ __forceinline__ uint64_t make_sw128_atom32_desc(uint32_t smem_addr, uint32_t lbo_bytes,
+                                                           uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(1u) << 61;
+  return d;
+}
+
 // 32-bit instruction descriptor for kind::f16 / kind::tf32 with fp32 accumulate.
 //   [4,6) D format (1 = f32)   [7,10) A format   [10,13) B format
 //   (f16 kind: 0 = f16, 1 = bf16; tf32 kind: 2 = tf32)

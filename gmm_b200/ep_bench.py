@@ -239,7 +239,7 @@ def run(args, metric, load_peaks, clock_sampler):
         cid = args.config or 2
         cfg = CONFIGS[cid]
         weak = cid == 2
-        s = _Setup(cfg, world, rank, dev, count_group, weak)
+        s = _Setup(cfg, world, rank, dev, count_group, weak, barrier=os.environ.get("GMM_EP_BARRIER", "flags"))
         for _ in range(max(3, args.warmup)):
             s.step()
         torch.cuda.synchronize()
@@ -299,7 +299,8 @@ def run(args, metric, load_peaks, clock_sampler):
         ep_configs = {}
         if not args.no_configs:
             for ecid in (5, 3):
-                es_ = _Setup(CONFIGS[ecid], world, rank, dev, count_group, weak=False)
+                es_ = _Setup(CONFIGS[ecid], world, rank, dev, count_group, weak=False,
+                             barrier=os.environ.get("GMM_EP_BARRIER", "flags"))
                 ms = es_.timed(max(3, min(args.steps, 20)), args.warmup)
                 entry = ep_config_entry(es_, ms, world)
                 entry["parity"] = es_.parity()

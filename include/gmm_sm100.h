@@ -17,7 +17,8 @@
  *   D[rows] = A[rows] @ B[e]        (B[e]^T when trans_b)
  * accumulated in fp32.  Zero-row experts are skipped.  fp32 inputs are
  * multiplied on the tensor cores as three TF32 products (hi*hi + hi*lo +
- * lo*hi) which gives close to fp32 accuracy.
+ * lo*hi, the split made in shared memory inside the GEMM kernel) which gives
+ * close to fp32 accuracy.
  */
 #ifndef GMM_SM100_H_
 #define GMM_SM100_H_
@@ -73,8 +74,8 @@ int gmm_sm100_set_tile_kind(int kind);
  * (reference csrc/hopper_gmm_forward.cu:389-397). */
 int gmm_sm100_check_device(int device);
 
-/* Bytes of device workspace gmm_sm100_forward needs for this problem; 0 for
- * bf16/fp16 with at most 1024 non-empty experts.  Replaces the reference's
+/* Bytes of device workspace gmm_sm100_forward needs for this problem: the
+ * tile table when more than 1024 experts are non-empty, else 0.  Replaces the reference's
  * workspace sizing (reference csrc/hopper_gmm_forward.cu:210-222, 411-427). */
 size_t gmm_sm100_workspace_size(const int64_t* batch_sizes, int64_t num_experts,
                                 int64_t num_tokens, int64_t dim, int64_t dim_out, int dtype,
@@ -152,12 +153,14 @@ int gmm_sm100_forward_vark(const void* A, const void* B, const int64_t* batch_si
  * written.  If a size is negative or the sum exceeds rows_cap the kernel does
  * no work and records GMM_ERR_INVALID_ARGUMENT / GMM_ERR_BATCH_SUM in the
  * device error word.  swiglu != 0 selects the fused SwiGLU epilogue (see
- * gmm_sm100_forward_swiglu).  Workspace: gmm_sm100_dev_workspace_size(). */
+ * gmm_sm100_forward_swiglu).  Needs no workspace: the group table is built in
+ * shared memory (workspace / workspace_bytes are accepted and ignored). */
 int gmm_sm100_forward_dev(const void* A, const void* B, const int32_t* batch_sizes_dev,
                           int64_t num_experts, int64_t rows_cap, int64_t dim, int64_t dim_out,
                           int dtype, int trans_b, int swiglu, void* D, void* workspace,
                           size_t workspace_bytes, void* stream);
 
+/* Workspace bytes gmm_sm100_forward_dev needs: 0 for every problem. */
 size_t gmm_sm100_dev_workspace_size(int64_t num_experts, int64_t rows_cap, int64_t dim,
                                     int64_t dim_out, int dtype);
 
@@ -270,23 +273,25 @@ size_t gmm_sm100_ep_workspace_size(const int64_t* counts, int64_t num_local_expe
  * cannot afford cudaMalloc / cudaFree, which may synchronise the whole device.
  *
  * Same arguments and results as gmm_sm100_forward with dtype GMM_DTYPE_F32
- * (three TF32 tensor-core products), minus the workspace: the hi/lo TF32
- * splits of A and B (and the tile table, for more than 1024 non-empty
- * experts) go to a scratch array of GMM_SM100_NOALLOC_SCRATCH_BYTES compiled
- * into the library, which every GPU that loads the library keeps until the
- * process exits.  Problems whose scratch need
- *   2*num_tokens*dim*4 + 2*num_experts*dim*dim_out*4  (each rounded up to 256 B)
- * exceeds that size are rejected with GMM_ERR_TOO_LARGE before any GPU work.
+ * (three TF32 tensor-core products, split into TF32 hi/lo parts in shared
+ * memory), minus the workspace: the one device buffer that path needs, the
+ * tile table of more than 1024 non-empty experts, goes to a scratch array of
+ * GMM_SM100_NOALLOC_SCRATCH_BYTES compiled into the library, which every GPU
+ * that loads the library keeps until the process exits.  Problems whose table
+ *   (3 * non-empty experts + 2) * 4 bytes, rounded up to 256
+ * exceeds that size (about 699,000 non-empty experts) are rejected with
+ * GMM_ERR_TOO_LARGE before any GPU work.
  *
- * The first call on a device looks up the scratch array's device address
- * (cudaGetSymbolAddress) with that device current; make that first call
- * before any stream capture.  The address is kept per device ordinal, so it
- * belongs to the device's primary context, the one every CUDA runtime call
- * works in; a caller that makes a different driver-API context current on
- * the device (cuCtxSetCurrent) must not use this entry point.  All calls share the one scratch array, and its
- * contents are fully rewritten by each call before they are read: calls whose
- * GPU work overlaps (different streams, or different host threads, on one
- * device) race on it and must be serialised by the caller. */
+ * The first call on a device that needs the scratch looks up the array's
+ * device address (cudaGetSymbolAddress) with that device current; make that
+ * first call before any stream capture.  The address is kept per device
+ * ordinal, so it belongs to the device's primary context, the one every CUDA
+ * runtime call works in; a caller that makes a different driver-API context
+ * current on the device (cuCtxSetCurrent) must not use this entry point.
+ * All calls share the one scratch array; each call writes the part it reads
+ * before its kernel runs (stream-ordered), so calls whose GPU work overlaps
+ * (different streams, or different host threads, on one device) race on it
+ * and must be serialised by the caller. */
 int gmm_sm100_forward_f32_noalloc(const float* A, const float* B, const int64_t* batch_sizes,
                                   int64_t num_experts, int64_t num_tokens, int64_t dim,
                                   int64_t dim_out, int trans_b, float* D, void* stream);

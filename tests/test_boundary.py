@@ -90,9 +90,9 @@ def test_cabi_errstr_and_workspace():
     assert lib.gmm_sm100_errstr(-100) == b"unknown status"
     # bf16/fp16 with a small table: no workspace
     assert capi.workspace_size([64] * 8, 512, 128, 256, capi.GMM_DTYPE_BF16, False) == 0
-    # fp32: hi/lo copies of A and B (each 256-byte rounded)
-    ws = capi.workspace_size([64] * 8, 512, 128, 256, capi.GMM_DTYPE_F32, False)
-    assert ws == 2 * 512 * 128 * 4 + 2 * 8 * 128 * 256 * 4
+    # fp32: none either (the TF32 hi/lo split is made in shared memory)
+    assert capi.workspace_size([64] * 8, 512, 128, 256, capi.GMM_DTYPE_F32, False) == 0
+    assert capi.workspace_size([64] * 8, 512, 128, 256, capi.GMM_DTYPE_F32, True) == 0
     # more than 1024 non-empty experts: the table moves to the workspace
     ws = capi.workspace_size([1] * 2000, 2000, 64, 64, capi.GMM_DTYPE_F16, True)
     assert ws == ((3 * 2000 + 2) * 4 + 255) // 256 * 256
@@ -135,9 +135,10 @@ def test_cabi_other_entries_validate_on_host():
     assert lib.gmm_sm100_forward_dev(P, P, P, 4, 8, 64, 64, 0, 0, 1, P, None, 0, None) == -1
     assert lib.gmm_sm100_forward_dev(P, P, P, 4, 8, 64, 64, 1, 0, 0, P + 8, None, 0, None) == -4
     assert lib.gmm_sm100_forward_dev(P, P, P + 2, 4, 8, 64, 64, 1, 0, 0, P, None, 0, None) == -4
-    # the allocation-free fp32 entry: a problem whose scratch exceeds the fixed array
-    big = np.asarray([1024], dtype=np.int64)
-    rc = lib.gmm_sm100_forward_f32_noalloc(P, P, big.ctypes.data, 1, 1024, 1024, 1024, 0, P, None)
+    # the allocation-free fp32 entry: a tile table (800,000 non-empty experts)
+    # larger than the fixed array
+    big = np.ones(800_000, dtype=np.int64)
+    rc = lib.gmm_sm100_forward_f32_noalloc(P, P, big.ctypes.data, big.shape[0], big.shape[0], 64, 64, 0, P, None)
     assert rc == -8 and "fixed scratch holds 8388608 bytes" in last()
     assert lib.gmm_sm100_forward_f32_noalloc(P, P, bs.ctypes.data, 2, 9, 64, 64, 0, P, None) == -2
     # routing and permutation

@@ -2,16 +2,16 @@
 
 It serves callers that cannot allocate device memory themselves (a plugin
 inside an engine that owns every allocation, or a caller that cannot let
-cudaMalloc / cudaFree synchronise the device): its scratch is a fixed array
-compiled into the library.  These tests drive it through the C ABI and check
-it against the regular entry point (``hopper_gmm_fwd`` -> ``gmm_sm100_forward``)
-at the fp32 tolerance used by every other test, on two calls in a row, so a
-second call that reuses the shared scratch is covered too.
+cudaMalloc / cudaFree synchronise the device): the one device buffer the fp32
+path can need -- the tile table of more than 1024 non-empty experts -- lives
+in a fixed array compiled into the library.  These tests drive it through the
+C ABI and check it against the CPU oracle at the fp32 tolerance used by every
+other test, and against the regular entry point, on two calls in a row (so a
+second call that reuses the shared array is covered too), including a
+problem whose table does go through the array.
 
 This file is named to be collected last.
 """
-
-import ctypes
 
 import numpy as np
 import pytest
@@ -42,29 +42,46 @@ def _device():
     torch.cuda.set_device(0)
 
 
+def _problem(g, bs, dim, dim_out, trans_b):
+    T = int(sum(bs))
+    a = torch.randn(T, dim, generator=g)
+    shape = (len(bs), dim_out, dim) if trans_b else (len(bs), dim, dim_out)
+    b = torch.randn(*shape, generator=g)
+    return a, b
+
+
 @pytest.mark.parametrize("trans_b", [False, True])
-def test_noalloc_matches_regular_entry_twice(trans_b):
+def test_noalloc_matches_oracle_and_regular_entry_twice(trans_b):
     from gmm_b200 import hopper_gmm_fwd
     g = torch.Generator().manual_seed(21)
-    problems = [([64, 0, 130, 1, 57], 192, 320), ([512] * 8, 128, 256)]
-    for bs, dim, dim_out in problems:  # two calls in a row on the shared scratch
-        T = sum(bs)
-        a = torch.randn(T, dim, generator=g).cuda()
-        shape = (len(bs), dim_out, dim) if trans_b else (len(bs), dim, dim_out)
-        b = torch.randn(*shape, generator=g).cuda()
-        d = torch.full((T, dim_out), float("nan"), device="cuda")
-        rc, msg = _noalloc(a, b, bs, trans_b, d)
+    many = torch.randint(1, 4, (1200,), generator=g)
+    many[::11] = 0  # 1090 non-empty experts, some empty ones between them
+    problems = [([64, 0, 130, 1, 57], 192, 320),  # inline tile table
+                (many.tolist(), 32, 64),           # more than 1024 non-empty experts: table in the array
+                ([512] * 8, 128, 256)]             # inline again, after the array was used
+    assert sum(1 for m in problems[1][0] if m > 0) > 1024
+    for bs, dim, dim_out in problems:  # calls in a row on the shared array
+        a, b = _problem(g, bs, dim, dim_out, trans_b)
+        d = torch.full((a.shape[0], dim_out), float("nan"), device="cuda")
+        rc, msg = _noalloc(a.cuda(), b.cuda(), bs, trans_b, d)
         assert rc == 0, msg
-        want = hopper_gmm_fwd(a, b, torch.tensor(bs), trans_b=trans_b)
         torch.cuda.synchronize()
-        ok, nbad, err = oracle.allclose_report(d.cpu().numpy(), want.cpu().numpy(), TOL)
-        assert ok, f"bs={bs}: {nbad} elements differ beyond {TOL}, max err {err}"
+        got = d.cpu().numpy()
+        want = oracle.gmm_oracle_c(a, b, bs, trans_b)
+        ok, nbad, err = oracle.allclose_report(got, want, TOL)
+        assert ok, f"{len(bs)} experts: {nbad} elements off the oracle beyond {TOL}, max err {err}"
+        regular = hopper_gmm_fwd(a.cuda(), b.cuda(), torch.tensor(bs), trans_b=trans_b).cpu().numpy()
+        ok, nbad, err = oracle.allclose_report(got, regular, TOL)
+        assert ok, f"{len(bs)} experts: {nbad} elements off the regular entry point, max err {err}"
 
 
-def test_noalloc_rejects_problems_beyond_its_scratch():
-    bs = [1024] * 8
-    a = torch.zeros(8192, 256, device="cuda")
-    b = torch.zeros(8, 256, 512, device="cuda")
-    d = torch.zeros(8192, 512, device="cuda")
+def test_noalloc_rejects_tables_beyond_its_array():
+    """800,000 one-row experts need a 9.6 MB tile table: more than the fixed
+    8 MiB array, so the call is rejected on the host, before any GPU work."""
+    E = 800_000
+    bs = np.ones(E, dtype=np.int64)
+    a = torch.zeros(E, 4, device="cuda")
+    b = torch.zeros(E, 4, 4, device="cuda")
+    d = torch.zeros(E, 4, device="cuda")
     rc, msg = _noalloc(a, b, bs, False, d)
     assert rc == -8 and "scratch" in msg
