@@ -75,9 +75,15 @@ CONFIGS = {
 }
 
 
-def route(cfg: GmmConfig, gen: torch.Generator, tokens: Optional[int] = None) -> torch.Tensor:
-    """Top-k expert ids ``[tokens, top_k]`` (int64, CPU) for ``cfg``'s routing law."""
+def route(cfg: GmmConfig, gen: torch.Generator, tokens: Optional[int] = None,
+          sample_gen: Optional[torch.Generator] = None) -> torch.Tensor:
+    """Top-k expert ids ``[tokens, top_k]`` (int64, CPU) for ``cfg``'s routing law.
+
+    ``sample_gen`` (zipf / dirichlet laws): draw the tokens' experts from it
+    instead of ``gen``, keeping the expert popularity ``gen`` fixes -- another
+    batch of the same model, as a load balancer's history would see it."""
     n_tok = cfg.tokens if tokens is None else tokens
+    sg = gen if sample_gen is None else sample_gen
     E, k = cfg.num_experts, cfg.top_k
     if cfg.routing == "uniform":
         # bs = [tokens/E]*E exactly: token t goes to expert t // (tokens/E).
@@ -93,13 +99,13 @@ def route(cfg: GmmConfig, gen: torch.Generator, tokens: Optional[int] = None) ->
         w = torch.empty(E, dtype=torch.float64)
         w[perm] = torch.arange(1, E + 1, dtype=torch.float64).pow(-1.1)
         w[perm[E - 16:]] = 0.0
-        return torch.multinomial(w.expand(n_tok, E), k, replacement=False, generator=gen)
+        return torch.multinomial(w.expand(n_tok, E), k, replacement=False, generator=sg)
     if cfg.routing == "dirichlet":
         conc = torch.full((E,), 5.0, dtype=torch.float64)
         # Dirichlet(alpha) = normalised Gamma(alpha, 1) draws.
         g = torch._standard_gamma(conc.unsqueeze(0).expand(1, E).contiguous(), generator=gen)[0]
         p = g / g.sum()
-        return torch.multinomial(p.expand(n_tok, E), k, replacement=False, generator=gen)
+        return torch.multinomial(p.expand(n_tok, E), k, replacement=False, generator=sg)
     raise ValueError(cfg.routing)
 
 
@@ -166,3 +172,13 @@ def workload_config(cfg: GmmConfig, world: int = 1, weak: bool = False) -> dict:
             "rows": tokens * cfg.top_k, "trans_b": cfg.trans_b, "parallelism": f"ep{world}",
             "scaling": "weak" if weak else "strong",
             "l2": l2_note(cfg, batch_sizes_for(cfg))}
+
+
+def history_loads(cfg: GmmConfig, tokens: Optional[int] = None) -> torch.Tensor:
+    """Rows per expert of another batch with the same expert popularity (a
+    different token sample): what a load balancer would have measured before
+    placing the experts.  ``[num_experts]`` int64."""
+    gen = torch.Generator().manual_seed(cfg.seed)
+    sample = torch.Generator().manual_seed(cfg.seed + 7777)
+    ids = route(cfg, gen, tokens=tokens, sample_gen=sample)
+    return torch.bincount(ids.flatten(), minlength=cfg.num_experts).to(torch.int64)

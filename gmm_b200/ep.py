@@ -43,7 +43,9 @@ Two transports carry steps 2 and 4:
 * ``"nccl"``: NCCL point-to-point messages (below); also what the CPU tests
   run on gloo ranks.
 
-Rank r owns experts ``[r*E/W, (r+1)*E/W)``.  Output rows are bit-identical
+Rank r owns experts ``[r*E/W, (r+1)*E/W)``; any other placement is a
+relabelling of the experts (label l = the expert placed in slot l, the rows
+grouped by label), e.g. ``balanced_placement`` of measured loads.  Output rows are bit-identical
 to the single-GPU operator on the same rows.  There is no CPU fallback: the
 local GEMM is the CUDA kernel (through the C ABI, writing in place into a
 reused buffer) unless a test substitutes the CPU oracle to check the
@@ -56,6 +58,26 @@ from typing import Callable, List, Optional
 
 import torch
 import torch.distributed as dist
+
+
+def balanced_placement(loads, world: int) -> List[int]:
+    """Expert placement for expert parallelism: ``perm[l]`` is the expert that
+    takes label ``l``, and rank r owns labels ``[r*E/W, (r+1)*E/W)``.  Experts
+    go, heaviest first, to the rank with the fewest rows so far among those with
+    a free slot (greedy longest-processing-time), so every rank computes about
+    the same number of rows."""
+    loads = [int(v) for v in loads]
+    E = len(loads)
+    if E % world:
+        raise ValueError(f"{E} experts do not split over {world} ranks")
+    per = E // world
+    rows = [0] * world
+    owned: List[List[int]] = [[] for _ in range(world)]
+    for e in sorted(range(E), key=lambda i: (-loads[i], i)):
+        r = min((r for r in range(world) if len(owned[r]) < per), key=lambda r: (rows[r], r))
+        owned[r].append(e)
+        rows[r] += loads[e]
+    return [e for r in range(world) for e in sorted(owned[r])]
 
 
 class _Chunking:
@@ -127,7 +149,12 @@ class ExpertParallelGmm:
         self._epoch = 0
         self._flags = None  # (symmetric int32 flag slots, their per-rank addresses, handle)
         self.record_phases = False  # when set, CUDA events around each phase of a direct step
-        self.phase_events = []
+        self.phase_events = {}
+        # direct transport: the own-rows GEMM overlaps the barrier + gather when this
+        # rank's own rows average at least overlap_min_rows per local expert
+        self.overlap = True
+        self.overlap_min_rows = 256
+        self._side = None
         self._sym = None  # (capacity rows, dim, dim_out, dtype, device, a_sym, out_sym, a_ptrs, out_ptrs)
         self._flag = None
         self.group = group
@@ -254,11 +281,11 @@ class ExpertParallelGmm:
         sym = self._symmetric(rows, dim, dim_out, dtype, device)
         return sym[6][:rows * dim_out].view(rows, dim_out)
 
-    def _mark(self, device):
+    def _mark(self, device, name):
         if self.record_phases:
             e = torch.cuda.Event(enable_timing=True)
             e.record(torch.cuda.current_stream(device))
-            self.phase_events.append(e)
+            self.phase_events[name] = e
 
     def _forward_direct(self, a, b_local, all_bs, trans_b, out=None):
         from gmm_b200 import capi
@@ -280,22 +307,67 @@ class ExpertParallelGmm:
         order = [(r + j) % W for j in range(W)]
         counts = all_bs[order][:, mine].t().contiguous().numpy()  # [El, W]
         rows_at = offs[order][:, mine].t().contiguous().numpy()   # where they sit on their rank
-        n_recv = int(counts.sum())
-        x = self._buffer("_x", n_recv, dim, a)
         if self.record_phases:
-            self.phase_events = []
-        self._mark(a.device)
-        self._barrier(a.device)  # every rank's token rows are in place
-        self._mark(a.device)
-        if n_recv:
-            capi.ep_gather(x, sym[7], counts, rows_at, El, dim * a.element_size(), rank_base=r)
-            self._mark(a.device)
-            capi.forward_ep(x, b_local, counts, rows_at, El, sym[8], trans_b=trans_b, rank_base=r)
-        else:
-            self._mark(a.device)
-        self._mark(a.device)
-        self._barrier(a.device)  # every peer's result rows have landed here
-        self._mark(a.device)
+            self.phase_events = {}
+        # Overlap only pays when the own-rows GEMM is compute-bound: it reads all
+        # local experts' weights a second time, which for a few rows per
+        # expert (HBM-bound) costs more than the gather it hides.
+        overlap = (self.overlap and W > 1
+                   and int(counts[:, 0].sum()) >= self.overlap_min_rows * El)
+        if not overlap:
+            n_recv = int(counts.sum())
+            x = self._buffer("_x", n_recv, dim, a)
+            self._mark(a.device, "start")
+            self._barrier(a.device)  # every rank's token rows are in place
+            self._mark(a.device, "barrier_in")
+            if n_recv:
+                capi.ep_gather(x, sym[7], counts, rows_at, El, dim * a.element_size(), rank_base=r)
+                self._mark(a.device, "gather")
+                capi.forward_ep(x, b_local, counts, rows_at, El, sym[8], trans_b=trans_b, rank_base=r)
+            self._mark(a.device, "peer_gemm")
+            self._barrier(a.device)  # every peer's result rows have landed here
+            self._mark(a.device, "barrier_out")
+            return self._result(res, out)
+        # Overlapped step.  This rank's own rows for its local experts are one
+        # contiguous block of its token rows: their GEMM (plain, local output)
+        # needs no exchange and runs on the compute stream while a side stream
+        # waits for the peers (barrier) and gathers their rows.  The peers'
+        # segments then go through the GEMM whose epilogue stores each row on
+        # its source rank.
+        own = counts[:, 0].copy()
+        o0 = int(offs[r, r * El])
+        n_own = int(own.sum())
+        peer = counts.copy()
+        peer[:, 0] = 0
+        n_peer = int(peer.sum())
+        x = self._buffer("_x", n_peer, dim, a)
+        main = torch.cuda.current_stream(a.device)
+        if self._side is None or self._side.device != a.device:
+            self._side = torch.cuda.Stream(device=a.device)
+        side = self._side
+        side.wait_stream(main)  # token rows written, previous step's reads of x done
+        self._mark(a.device, "start")
+        with torch.cuda.stream(side):
+            if W > 1:
+                self._barrier(a.device)  # every rank's token rows are in place
+            self._mark(a.device, "barrier_in")
+            if n_peer:
+                capi.ep_gather(x, sym[7], peer, rows_at, El, dim * a.element_size(), rank_base=r)
+            self._mark(a.device, "gather")
+        if n_own:
+            capi.forward(a_sym[o0:o0 + n_own], b_local, own, res[o0:o0 + n_own], trans_b=trans_b)
+        self._mark(a.device, "own_gemm")
+        main.wait_stream(side)
+        if n_peer:
+            capi.forward_ep(x, b_local, peer, rows_at, El, sym[8], trans_b=trans_b, rank_base=r)
+        self._mark(a.device, "peer_gemm")
+        if W > 1:
+            self._barrier(a.device)  # every peer's result rows have landed here
+        self._mark(a.device, "barrier_out")
+        return self._result(res, out)
+
+    @staticmethod
+    def _result(res, out):
         if out is None:
             return res.clone()
         if out.data_ptr() != res.data_ptr():
@@ -304,12 +376,13 @@ class ExpertParallelGmm:
 
     def phase_ms(self):
         """Milliseconds of the last direct step's phases (``record_phases`` must
-        have been set): barrier before, gather, GEMM + combine, barrier after."""
+        have been set), each from the step's start: when the entry barrier, the
+        gather, the own-rows GEMM, the peer-rows GEMM (+ combine) and the exit
+        barrier had finished."""
         ev = self.phase_events
-        if len(ev) != 5:
+        if not ev or "start" not in ev:
             return None
-        return {name: ev[i].elapsed_time(ev[i + 1])
-                for i, name in enumerate(("barrier_in", "gather", "gemm_combine", "barrier_out"))}
+        return {k: ev["start"].elapsed_time(e) for k, e in ev.items() if k != "start"}
 
     # --------------------------------------------------------------- forward
     def forward(self, a: torch.Tensor, b_local: torch.Tensor, batch_sizes: torch.Tensor,

@@ -14,8 +14,11 @@ of the north star, strong-scaled --
 * cfg3 (DeepSeek-V3 shapes, fp16 NT): 4096 tokens in total, 256/N experts
   per rank --
 
-each with its step time, tokens/s, whole-job TFLOP/s, the load-imbalance
-ceiling of its routing (mean / max rows computed per rank) and ``parity``:
+with the experts placed by load (``balanced_placement`` of another batch's
+routed rows; ``GMM_EP_PLACEMENT=contiguous`` for E/N-expert blocks), each with
+its step time, tokens/s, whole-job TFLOP/s, the load-imbalance ceiling of its
+routing (mean / max rows computed per rank, also for contiguous blocks) and
+``parity``:
 sampled output rows of every rank, two or more per global expert (so every
 rank's local experts are covered), against a plain PyTorch fp32 reference on
 the GPU at the north-star tolerance.
@@ -83,13 +86,20 @@ def check_parity(out, a, bs, get_b, trans_b, rows_per_expert=2, seed=0, max_expe
 
 
 # ------------------------------------------------------------------ workloads
-def routing(cfg, world, rank, weak):
-    """This rank's token shard of one global routing draw (same on every rank)."""
+def routing(cfg, world, rank, weak, perm=None):
+    """This rank's token shard of one global routing draw (same on every rank).
+
+    ``perm`` (an expert placement, ``perm[label] = expert``): expert ids are
+    relabelled so that rank r's experts are labels ``[r*E/W, (r+1)*E/W)``."""
     from gmm_b200.configs import route
     tokens_r = cfg.tokens if weak else cfg.tokens // world
     total = tokens_r * world
     gen = torch.Generator().manual_seed(cfg.seed)
     ids = route(cfg, gen, tokens=total)
+    if perm is not None:
+        inv = torch.empty(len(perm), dtype=torch.int64)
+        inv[torch.as_tensor(perm)] = torch.arange(len(perm))
+        ids = inv[ids]
     bs_all = [torch.bincount(ids[r * tokens_r:(r + 1) * tokens_r].flatten(),
                              minlength=cfg.num_experts).to(torch.int64) for r in range(world)]
     return bs_all[rank], tokens_r, total, torch.stack(bs_all)
@@ -132,18 +142,25 @@ def _sum_over_ranks(v, dev):
 class _Setup:
     """One expert-parallel workload on this rank: routing, weights, inputs, layer."""
 
-    def __init__(self, cfg, world, rank, dev, count_group, weak, barrier="flags"):
-        from gmm_b200.ep import ExpertParallelGmm
+    def __init__(self, cfg, world, rank, dev, count_group, weak, barrier="flags", placement="contiguous"):
+        from gmm_b200.configs import history_loads
+        from gmm_b200.ep import ExpertParallelGmm, balanced_placement
         self.cfg, self.world, self.rank, self.dev = cfg, world, rank, dev
         E = cfg.num_experts
         if E % world:
             raise SystemExit(f"cfg{cfg.cid}: {E} experts do not split over {world} ranks")
         self.El = El = E // world
-        self.bs, self.tokens_r, self.tokens_total, all_bs = routing(cfg, world, rank, weak)
+        # expert placement: label l is expert perm[l]; rank r owns labels [r*El, (r+1)*El)
+        self.placement = placement
+        self.perm = (balanced_placement(history_loads(cfg), world) if placement == "balanced"
+                     else list(range(E)))
+        self.bs, self.tokens_r, self.tokens_total, all_bs = routing(
+            cfg, world, rank, weak, self.perm if placement == "balanced" else None)
         self.rows_r = int(self.bs.sum())
-        self.b_local = local_weights(cfg, list(range(rank * El, (rank + 1) * El)), dev)
+        self.b_local = local_weights(cfg, [self.perm[l] for l in range(rank * El, (rank + 1) * El)], dev)
         self.ep = ExpertParallelGmm(E, count_group=count_group,
                                     transport=os.environ.get("GMM_EP_TRANSPORT", "auto"), barrier=barrier)
+        self.ep.overlap = os.environ.get("GMM_EP_OVERLAP", "1") != "0"
         self.all_bs = self.ep.exchange_counts(self.bs)
         assert torch.equal(self.all_bs, all_bs), "count exchange disagrees with the routing draw"
         g = torch.Generator(device=dev).manual_seed(cfg.seed * 7919 + rank)
@@ -164,6 +181,9 @@ class _Setup:
         per_rank = self.all_bs.view(world, world, El).sum(dim=(0, 2)).double()
         self.imbalance = {"rows_per_rank_max": int(per_rank.max()), "rows_per_rank_mean": float(per_rank.mean()),
                           "efficiency_ceiling": round(float(per_rank.mean() / per_rank.max()), 4)}
+        if placement == "balanced":  # what the contiguous placement would have given
+            contig = routing(cfg, world, rank, weak)[3].view(world, world, El).sum(dim=(0, 2)).double()
+            self.imbalance["efficiency_ceiling_contiguous"] = round(float(contig.mean() / contig.max()), 4)
 
     def step(self):
         return self.ep(self.a, self.b_local, self.bs, self.cfg.trans_b, all_bs=self.all_bs, out=self.out)
@@ -187,10 +207,10 @@ class _Setup:
         """This rank's output rows (the last step's) for every global expert."""
         cfg, El = self.cfg, self.El
 
-        def get_b(e):
-            if self.rank * El <= e < (self.rank + 1) * El:
-                return self.b_local[e - self.rank * El]
-            return expert_weight(cfg, e, self.dev)
+        def get_b(label):
+            if self.rank * El <= label < (self.rank + 1) * El:
+                return self.b_local[label - self.rank * El]
+            return expert_weight(cfg, self.perm[label], self.dev)
 
         res = check_parity(self.out, self.a, self.bs.tolist(), get_b, cfg.trans_b, seed=self.rank)
         ok = _sum_over_ranks(0 if res["ok"] else 1, self.dev) == 0
@@ -217,6 +237,9 @@ def ep_config_entry(setup, ms, world):
     cfg = setup.cfg
     return {"workload": f"cfg{cfg.cid}: {cfg.name}", "dtype": _dtype_name(cfg.dtype),
             "scaling": "strong", "tokens": setup.tokens_total, "experts_per_rank": setup.El,
+            "placement": ("load-balanced: experts placed heaviest-first on the least-loaded rank, "
+                          "by the routed rows of another batch of the same expert popularity"
+                          if setup.placement == "balanced" else "contiguous blocks of E/N experts"),
             "ms_per_step": round(ms, 4), "tokens_per_s": round(setup.tokens_total / (ms * 1e-3), 1),
             "tflops": round(setup.flops / (ms * 1e-3) / 1e12, 2), "n_gpus": world,
             "load_imbalance": setup.imbalance}
@@ -290,6 +313,8 @@ def run(args, metric, load_peaks, clock_sampler):
         d2h = _sum_over_ranks(s.rows_r * cfg.dim_out * es, dev)
         head_imb = s.imbalance
         transport = s.direct
+        overlap = s.ep.overlap
+        barrier_kind = "flag-kernel" if s.ep.barrier == "flags" else "NCCL all-reduce"
         shm = s.ep._shm_counts is not None
         flops, tokens_total, rows_total, El = s.flops, s.tokens_total, s.rows_total, s.El
         s.close()
@@ -300,7 +325,8 @@ def run(args, metric, load_peaks, clock_sampler):
         if not args.no_configs:
             for ecid in (5, 3):
                 es_ = _Setup(CONFIGS[ecid], world, rank, dev, count_group, weak=False,
-                             barrier=os.environ.get("GMM_EP_BARRIER", "flags"))
+                             barrier=os.environ.get("GMM_EP_BARRIER", "flags"),
+                             placement=os.environ.get("GMM_EP_PLACEMENT", "balanced"))
                 ms = es_.timed(max(3, min(args.steps, 20)), args.warmup)
                 entry = ep_config_entry(es_, ms, world)
                 entry["parity"] = es_.parity()
@@ -326,15 +352,19 @@ def run(args, metric, load_peaks, clock_sampler):
                 "ep": {"experts_per_rank": El, "rows": int(rows_total),
                        "exchange": (("shared-memory" if shm else "gloo") + " count all-gather; "
                                     + ("NVLink peer-load gather + combine fused into the GEMM "
-                                       "epilogue (symmetric memory), flag barriers" if transport
-                                       else "NCCL P2P dispatch/combine")),
+                                       "epilogue (symmetric memory); own-rows GEMM overlapping the "
+                                       "gather" if transport and overlap else
+                                       "NVLink peer-load gather + combine fused into the GEMM "
+                                       "epilogue (symmetric memory)" if transport
+                                       else "NCCL P2P dispatch/combine")
+                                    + f"; {barrier_kind} barriers"),
                        "load_imbalance": head_imb},
                 "parity": head_parity,
                 "e2e": {"value": round(flops / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
                         "ms_per_step": round(e2e_ms, 3),
                         "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                         "path": "pinned host A_r, B_local -> device; EP forward; out -> pinned host"},
-                "gpu_launches": args.steps * (4 if transport else 1),
+                "gpu_launches": args.steps * (5 if transport and overlap else 4 if transport else 1),
                 "roofline": {"bound": "tensor", "achieved": round(per_gpu, 2),
                              "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                              "frac": round(per_gpu / peaks["bf16_tflops"], 4), "traffic": None,

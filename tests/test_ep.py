@@ -176,3 +176,21 @@ def test_shared_memory_count_exchange_and_its_timeout():
         mp.spawn(_shm_worker, args=(2, _free_port(), d), nprocs=2, join=True)
         status = open(os.path.join(d, "rank0.txt")).read()
         assert status.startswith("raised") and "did not post" in status, status
+
+
+def test_balanced_placement_is_a_permutation_that_balances():
+    """balanced_placement: a permutation giving every rank E/W experts, and on
+    cfg3's Zipf routing (placed by another batch's loads) a far better
+    mean/max row ratio than contiguous blocks."""
+    from gmm_b200.configs import CONFIGS, batch_sizes_for, history_loads
+    from gmm_b200.ep import balanced_placement
+    cfg = CONFIGS[3]
+    real = batch_sizes_for(cfg)
+    perm = balanced_placement(history_loads(cfg), 8)
+    assert sorted(perm) == list(range(cfg.num_experts))
+    El = cfg.num_experts // 8
+    rows = torch.stack([real[perm[r * El:(r + 1) * El]].sum() for r in range(8)]).double()
+    contiguous = real.view(8, El).sum(1).double()
+    assert rows.mean() / rows.max() > 0.95 > contiguous.mean() / contiguous.max()
+    with pytest.raises(ValueError):
+        balanced_placement([1, 2, 3], 2)

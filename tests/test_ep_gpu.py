@@ -52,7 +52,10 @@ def _worker(rank, world, port, E, dtype, trans_b, transport, tile):
         ep = ExpertParallelGmm(E, transport=transport)
         b_local = b_full[rank * El:(rank + 1) * El].contiguous()
         want = hopper_gmm_fwd(a, b_full, bs, trans_b=trans_b)
-        for step in range(2):  # a second step reuses every buffer
+        ep.overlap_min_rows = 0  # overlap the own-rows GEMM with the gather whatever the sizes
+        for step in range(3):  # later steps reuse every buffer; the last runs without overlap
+            if step == 2:
+                ep.overlap = False
             out = ep(a, b_local, bs, trans_b)
             torch.cuda.synchronize()
             assert torch.equal(out, want), f"rank {rank} step {step}: EP differs from the single-GPU op"
