@@ -74,6 +74,10 @@ def parse():
     ap.add_argument("--phases", action="store_true",
                     help="N > 1: also time each phase of one expert-parallel step (barriers, gather, "
                          "GEMM + combine), max over ranks")
+    ap.add_argument("--cublas", action="store_true",
+                    help="N = 1: the configuration against cuBLAS (torch.matmul) per expert and as one GEMM")
+    ap.add_argument("--cublas-variant", choices=["ours", "cublas_per", "cublas_one"], default=None,
+                    help="with --cublas: time only this variant")
     ap.add_argument("--kernel-only", action="store_true",
                     help="warm-up + timed launches only (no e2e / CPU baseline / clocks): the "
                          "command profiled with ncu")
@@ -528,6 +532,58 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_cublas(args):
+    """The configuration's grouped GEMM against cuBLAS on the same shapes, in one
+    process: ``hopper_gmm_fwd``; ``torch.matmul`` per expert (the same work in E
+    launches); ``torch.matmul`` of all rows with one expert's B (no grouping, no
+    ragged tails: an upper bound for any grouped kernel).  Two passes of
+    event-timed loops (the second runs hotter, nearer the power cap)."""
+    import torch
+    from gmm_b200 import hopper_gmm_fwd
+    W = _workloads()
+    cid = args.config or 2
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg, bs, a, b = _config_inputs(W, cid, dev)
+    if args.max_experts:  # a smaller case of the same workload (the first experts and their rows)
+        import dataclasses
+        bs = bs[:args.max_experts].clone()
+        rows = int(bs.sum())
+        a, b = a[:rows], b[:args.max_experts]
+        cfg = dataclasses.replace(cfg, num_experts=len(bs), tokens=rows, top_k=1)
+    offs = [0]
+    for m in bs.tolist():
+        offs.append(offs[-1] + m)
+    out = torch.empty(cfg.rows, cfg.dim_out, dtype=cfg.dtype, device=dev)
+    bt = (lambda e: b[e].t()) if cfg.trans_b else (lambda e: b[e])  # noqa: E731
+
+    def ours():
+        hopper_gmm_fwd(a, b, bs, cfg.trans_b)
+
+    def per_expert():
+        for e in range(cfg.num_experts):
+            if offs[e + 1] > offs[e]:
+                torch.matmul(a[offs[e]:offs[e + 1]], bt(e), out=out[offs[e]:offs[e + 1]])
+
+    def one_gemm():
+        torch.matmul(a, bt(0), out=out)
+
+    steps = max(5, min(args.steps, 50))
+    res = {}
+    variants = (("ours_grouped", ours), ("cublas_per_expert", per_expert),
+                ("cublas_one_gemm_all_rows", one_gemm))
+    if args.cublas_variant:  # one variant only (the command an ncu capture runs)
+        variants = tuple(v for v in variants if v[0].startswith(args.cublas_variant))
+    for rep in ((1,) if args.cublas_variant else (1, 2)):
+        for name, fn in variants:
+            for _ in range(max(3, args.warmup)):
+                fn()
+            ms = statistics.fmean(_events_time(fn, steps))
+            res.setdefault(name, []).append({"pass": rep, "ms": round(ms, 4),
+                                             "tflops": round(cfg.flops() / (ms * 1e-3) / 1e12, 1)})
+    print(json.dumps({"workload": f"cfg{cid}: {cfg.name}", "steps": steps, "results": res}), flush=True)
+
+
 def run_ffn(args):
     """MoE expert FFN forward: SwiGLU(A @ W1) @ W2 over the config's expert segments."""
     import torch
@@ -664,6 +720,9 @@ def main():
         return
     if args.ffn and args.impl == "ours":
         run_ffn(args)
+        return
+    if args.cublas and args.impl == "ours":
+        run_cublas(args)
         return
     if args.impl == "reference":
         run_reference(args)
