@@ -90,11 +90,6 @@ struct __align__(64) GmmParams {
   int vk_m;        // variable-K kernel: rows of each D[e] (= columns of A)
   int vk_m_tiles;  // variable-K kernel: 128-row tiles per D[e]
   int ep_rank_base;  // remote mode: segment j of a group comes from rank (ep_rank_base + j) % world
-  // Interleaved walk of the 128-row kernel (mix_heavy_tiles > 0): the inline
-  // table holds, from int offset mix_off, the heavy groups' ids [nh] and m-tile
-  // prefix [nh+1], then the light groups' ids [nl] and prefix [nl+1].
-  int mix_off, mix_nh, mix_nl;
-  long long mix_heavy_tiles;
   // Bounded waits: limit of every pipeline wait (0 = kWaitTimeoutNs).  Test
   // hook of the timeout path: drop_kb1 = k + 1 > 0 makes the producer(s) of
   // the first tile of CTA (pair) 0 skip the loads of k-block k, so that the
@@ -273,47 +268,12 @@ struct Tile {
 };
 
 template <int BM, int BN>
-__device__ __forceinline__ Tile decode_group_tile(const TableView& t, int n_tiles, int g, int local);
-
-template <int BM, int BN>
 __device__ __forceinline__ Tile decode_tile(const TableView& t, int n_tiles, int tile, int& g) {
   // Groups are visited in increasing order by every CTA, so a forward scan
   // from the previous group finds the owner in amortised O(1).
   while (tile >= t.tile_off[g + 1] * n_tiles) ++g;
-  return decode_group_tile<BM, BN>(t, n_tiles, g, tile - t.tile_off[g] * n_tiles);
-}
-
-// Interleaved walk: position `pos` of the walk takes the next tile of a heavy
-// group (several m-tiles: B reused through L2, bound by the tensor cores) or
-// of a light group (one m-tile: streams its B from HBM), heavy and light in
-// proportion to their counts, so that every moment of the launch has both
-// kinds of work in flight instead of a compute phase and a streaming phase.
-// Each kind keeps its own forward-scan cursor (ch, cl).
-template <int BM, int BN>
-__device__ __forceinline__ Tile decode_mixed(const GmmParams& p, const TableView& t, const int32_t* tab,
-                                            int n_tiles, long long total, int pos, int& ch, int& cl,
-                                            int& g) {
-  const long long H = p.mix_heavy_tiles;
-  const long long before = (static_cast<long long>(pos) * H) / total;  // heavy tiles before pos
-  const int32_t* hgid = tab + p.mix_off;
-  const int32_t* htoff = hgid + p.mix_nh;
-  const int32_t* lgid = htoff + p.mix_nh + 1;
-  const int32_t* ltoff = lgid + p.mix_nl;
-  if ((static_cast<long long>(pos + 1) * H) / total > before) {
-    const int j = static_cast<int>(before);
-    while (j >= htoff[ch + 1] * n_tiles) ++ch;
-    g = hgid[ch];
-    return decode_group_tile<BM, BN>(t, n_tiles, g, j - htoff[ch] * n_tiles);
-  }
-  const int j = pos - static_cast<int>(before);
-  while (j >= ltoff[cl + 1] * n_tiles) ++cl;
-  g = lgid[cl];
-  return decode_group_tile<BM, BN>(t, n_tiles, g, j - ltoff[cl] * n_tiles);
-}
-
-template <int BM, int BN>
-__device__ __forceinline__ Tile decode_group_tile(const TableView& t, int n_tiles, int g, int local) {
   const int mt = t.tile_off[g + 1] - t.tile_off[g];
+  const int local = tile - t.tile_off[g] * n_tiles;
   // Raster: blocks of up to kMBlock m-tiles; inside a block m varies fastest so
   // the CTAs working on one B column panel run at the same time (L2 reuse).
   const int blk = local / (kMBlock * n_tiles);
@@ -568,11 +528,9 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_persistent_kernel(const __gri
       int issued[C::kStages];
       for (int s = 0; s < C::kStages; ++s) issued[s] = 0;
       bool ok = true;
-      int g = 0, ch = 0, cl = 0;
+      int g = 0;
       for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
-        const Tile t = p.mix_heavy_tiles
-                           ? decode_mixed<C::BM, C::BN>(p, tv, tab, n_tiles, total_tiles, tile, ch, cl, g)
-                           : decode_tile<C::BM, C::BN>(tv, n_tiles, tile, g);
+        const Tile t = decode_tile<C::BM, C::BN>(tv, n_tiles, tile, g);
         for (int kb = 0; kb < k_blocks; ++kb) {
           if (!mbar_wait(smem_u32(empty_bar + stage), phase ^ 1, abort_flag, wait_ns)) {
             ok = false;
@@ -735,16 +693,14 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_persistent_kernel(const __gri
         typename std::conditional<kKind == kKindBf16, __nv_bfloat16, __half>::type>::type;
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
     const uint32_t stage = smem_u32(epi_stage) + quarter * (32 * 128);
-    int g = 0, ch = 0, cl = 0;
+    int g = 0;
     int local = 0;
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++local) {
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(smem_u32(tfull_bar + acc), acc_phase, abort_flag, wait_ns)) break;
       tc_fence_after();
-      const Tile t = p.mix_heavy_tiles
-                         ? decode_mixed<C::BM, C::BN>(p, tv, tab, n_tiles, total_tiles, tile, ch, cl, g)
-                         : decode_tile<C::BM, C::BN>(tv, n_tiles, tile, g);
+      const Tile t = decode_tile<C::BM, C::BN>(tv, n_tiles, tile, g);
       if (quarter * 32 < t.rows) {  // warp-uniform: some row of this quarter is live
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * C::BN;
         if constexpr (!C::kTf32) {
@@ -1238,40 +1194,6 @@ int plan_impl(const int64_t* batch_sizes, int64_t num_experts, int64_t num_token
   return GMM_OK;
 }
 
-// Interleaved walk for problems with both heavy groups (several m-tiles) and
-// light groups (one m-tile), when both hold at least 1/8 of the tiles and the
-// lists fit after the inline table (see decode_mixed).
-void add_mix_lists(GmmParams& prm, const Plan& pl) {
-  const int G = pl.num_groups;
-  const int32_t* tile_off = pl.table.data() + G + 1;
-  std::vector<int32_t> hg, ht{0}, lg, lt{0};
-  for (int g = 0; g < G; ++g) {
-    const int mt = tile_off[g + 1] - tile_off[g];
-    if (mt >= 2) {
-      hg.push_back(g);
-      ht.push_back(ht.back() + mt);
-    } else {
-      lg.push_back(g);
-      lt.push_back(lt.back() + mt);
-    }
-  }
-  const long long heavy = static_cast<long long>(ht.back()) * pl.n_tiles;
-  const long long total = static_cast<long long>(pl.total_tiles);
-  const size_t off = pl.table.size();
-  const size_t need = hg.size() + ht.size() + lg.size() + lt.size();
-  if (heavy * 8 < total || (total - heavy) * 8 < total || off + need > static_cast<size_t>(kInlineTableInts))
-    return;
-  int32_t* dst = prm.inline_table + off;
-  for (auto* v : {&hg, &ht, &lg, &lt}) {
-    std::memcpy(dst, v->data(), v->size() * sizeof(int32_t));
-    dst += v->size();
-  }
-  prm.mix_off = static_cast<int>(off);
-  prm.mix_nh = static_cast<int>(hg.size());
-  prm.mix_nl = static_cast<int>(lg.size());
-  prm.mix_heavy_tiles = heavy;
-}
-
 // Test hook of the bounded-wait path (gmm_sm100_forward_inject_timeout).
 struct InjectTimeout {
   int drop_k_block;
@@ -1357,7 +1279,6 @@ int launch_impl(const PlanObj& po, const Plan& pl, const void* A, const void* B,
   if (pl.table_bytes == 0) {
     std::memcpy(prm.inline_table, pl.table.data(), pl.table.size() * sizeof(int32_t));
     prm.ext_table = nullptr;
-    if (kind == kTile128 && !inject) add_mix_lists(prm, pl);
   } else {
     ce = cudaMemcpyAsync(workspace, pl.table.data(), pl.table.size() * sizeof(int32_t), cudaMemcpyHostToDevice,
                          stream);
