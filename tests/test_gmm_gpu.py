@@ -366,3 +366,23 @@ def test_concurrent_host_threads_on_their_own_streams():
     for t in threads:
         t.join()
     assert not errors, errors
+
+
+@pytest.mark.parametrize("max_rows", [16, 32, 64, 128])
+@pytest.mark.parametrize("trans_b", [False, True])
+def test_swap_row_blocks(max_rows, trans_b):
+    """Swap-AB tiles whose tallest row block is 16, 32, 64 or 128 rows (the
+    MMA's N), zero-row experts between them, against the oracle."""
+    g = torch.Generator().manual_seed(max_rows)
+    bs = torch.randint(1, max_rows + 1, (40,), generator=g)
+    bs[3] = max_rows
+    bs[::9] = 0
+    T, dim, dim_out = int(bs.sum()), 320, 520
+    a = torch.randn(T, dim, generator=g).to(torch.bfloat16)
+    shape = (len(bs), dim_out, dim) if trans_b else (len(bs), dim, dim_out)
+    b = (torch.randn(*shape, generator=g) / dim ** 0.5).to(torch.bfloat16)
+    with forced_tile("swap"):
+        out = _fwd(a.cuda(), b.cuda(), bs, trans_b).cpu()
+    want = oracle.round_to(oracle.gmm_oracle_c(a, b, bs, trans_b), "bf16")
+    ok, nbad, err = oracle.allclose_report(out.float().numpy(), want, oracle.TOLERANCE["bf16"])
+    assert ok, (max_rows, nbad, err)
