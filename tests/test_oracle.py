@@ -51,11 +51,19 @@ def test_oracles_match_reference_ref_gmm(case):
 
 
 def test_ref_gmm_port_matches_reference():
+    """The literal torch-CPU port reproduces the reference's own outputs.  It
+    runs the same bf16 matmuls as the reference's ref_gmm, so on the CPU the
+    golden vectors were made on it is bit-identical; another CPU's BLAS may
+    order the fp32 accumulation differently and round a rare element to the
+    neighbouring bf16 value (seen: 1 element in 6,560 on an AMD EPYC host)."""
     case = next(c for c in CASES if c["name"] == "ragged_bf16_NT")
     a, b, bs = make_case_inputs(case)
     rows = GOLD[case["name"] + "__rows"]
     got = oracle.ref_gmm_port(a, b, bs, True)[rows].float().numpy()
-    np.testing.assert_array_equal(got, _golden_values(case))
+    want = _golden_values(case)
+    assert np.mean(got == want) > 0.999
+    ulp = np.exp2(np.floor(np.log2(np.maximum(np.abs(want), 1e-30))) - 7)  # bf16 spacing at |want|
+    assert np.all(np.abs(got - want) <= ulp)
 
 
 def test_oracle_rejects_bad_sum():
