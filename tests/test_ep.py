@@ -194,4 +194,3 @@ def test_balanced_placement_is_a_permutation_that_balances():
     assert rows.mean() / rows.max() > 0.95 > contiguous.mean() / contiguous.max()
     with pytest.raises(ValueError):
         balanced_placement([1, 2, 3], 2)
-
