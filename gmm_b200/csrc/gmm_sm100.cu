@@ -477,11 +477,17 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_persistent_kernel(const __gri
   uint8_t* epi_stage = smem + C::kStages * C::kStageBytes + C::kBarBytes;
   static_assert((3 * C::kStages + 6) * 8 <= C::kBarBytes, "barrier area");
 
+  // fp32: warps 2-3 split every landed stage into TF32 hi/lo.  A CTA that owns
+  // a single tile (a small, latency-bound problem) also lends its four
+  // epilogue warps to the split, which they finish before their one
+  // accumulator can be ready: six warps instead of two per stage.
+  const int conv_warps =
+      (C::kTf32 && p.dev_bs == nullptr && blockIdx.x + gridDim.x >= p.total_tiles) ? 6 : 2;
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(smem_u32(full_bar + s), 1);
       mbar_init(smem_u32(empty_bar + s), 1);
-      mbar_init(smem_u32(conv_bar + s), 2);
+      mbar_init(smem_u32(conv_bar + s), conv_warps);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(smem_u32(tfull_bar + a), 1);
@@ -519,6 +525,55 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_persistent_kernel(const __gri
     tab = dtab;
   }
   const TableView tv = make_table_view(p, tab, num_groups);
+
+  // ------------------------------------------------------------ fp32 split (converter)
+  // Each landed fp32 stage is split in shared memory: x -> hi (low 13
+  // mantissa bits cleared, exact in TF32) in place, x - hi -> the stage's lo
+  // copy at the same offset.  The split is element-wise, so the swizzled
+  // layout is preserved; the writes are fenced into the async proxy before
+  // the MMA warp (which waits on conv_bar for all conv_warps) hands them to
+  // the tensor cores.  Run by warps 2 .. 1 + conv_warps, thread ct of
+  // 32 * conv_warps taking every such 16-byte chunk of the stage.
+  auto split_stages = [&]() {
+    const int ct = threadIdx.x - 64;
+    const int nthr = 32 * conv_warps;
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
+      for (int kb = 0; kb < k_blocks; ++kb) {
+        if (!mbar_wait(smem_u32(full_bar + stage), phase, abort_flag, wait_ns)) {
+          ok = false;
+          break;
+        }
+        const uint32_t base = smem_u32(smem + stage * C::kStageBytes);
+        constexpr int kChunksA = C::kABytes / 16, kChunks = (C::kABytes + C::kBBytes) / 16;
+#pragma unroll 4
+        for (int i = ct; i < kChunks; i += nthr) {
+          // A: x at [0, kABytes), lo at [kABytes, 2 kABytes); B: x at 2 kABytes, lo kBBytes further
+          const uint32_t off = i < kChunksA ? i * 16 : 2 * C::kABytes + (i - kChunksA) * 16;
+          const uint32_t lo_off = off + (i < kChunksA ? C::kABytes : C::kBBytes);
+          const uint4 v = ld_shared_v4(base + off);
+          float h0, h1, h2, h3, l0, l1, l2, l3;
+          split_tf32(__uint_as_float(v.x), h0, l0);
+          split_tf32(__uint_as_float(v.y), h1, l1);
+          split_tf32(__uint_as_float(v.z), h2, l2);
+          split_tf32(__uint_as_float(v.w), h3, l3);
+          st_shared_v4(base + off, make_uint4(__float_as_uint(h0), __float_as_uint(h1), __float_as_uint(h2),
+                                              __float_as_uint(h3)));
+          st_shared_v4(base + lo_off, make_uint4(__float_as_uint(l0), __float_as_uint(l1), __float_as_uint(l2),
+                                                 __float_as_uint(l3)));
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(conv_bar + stage));
+        if (++stage == C::kStages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+  };
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -644,50 +699,11 @@ __global__ void __launch_bounds__(kThreads, 1) gmm_persistent_kernel(const __gri
       mbar_wait_drain(smem_u32(drain_bar), 0);
     }
   } else if (C::kTf32 && (warp == 2 || warp == 3)) {
-    // ------------------------------------------------------------ fp32 split (converter)
-    // Each landed fp32 stage is split in shared memory: x -> hi (low 13
-    // mantissa bits cleared, exact in TF32) in place, x - hi -> the stage's lo
-    // copy at the same offset.  The split is element-wise, so the swizzled
-    // layout is preserved; the writes are fenced into the async proxy before
-    // the MMA warp (which waits on conv_bar) hands them to the tensor cores.
-    const int ct = threadIdx.x - 64;  // 0..63
-    int stage = 0;
-    uint32_t phase = 0;
-    bool ok = true;
-    for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
-      for (int kb = 0; kb < k_blocks; ++kb) {
-        if (!mbar_wait(smem_u32(full_bar + stage), phase, abort_flag, wait_ns)) {
-          ok = false;
-          break;
-        }
-        const uint32_t base = smem_u32(smem + stage * C::kStageBytes);
-        constexpr int kChunksA = C::kABytes / 16, kChunks = (C::kABytes + C::kBBytes) / 16;
-#pragma unroll 4
-        for (int i = ct; i < kChunks; i += 64) {
-          // A: x at [0, kABytes), lo at [kABytes, 2 kABytes); B: x at 2 kABytes, lo kBBytes further
-          const uint32_t off = i < kChunksA ? i * 16 : 2 * C::kABytes + (i - kChunksA) * 16;
-          const uint32_t lo_off = off + (i < kChunksA ? C::kABytes : C::kBBytes);
-          const uint4 v = ld_shared_v4(base + off);
-          float h0, h1, h2, h3, l0, l1, l2, l3;
-          split_tf32(__uint_as_float(v.x), h0, l0);
-          split_tf32(__uint_as_float(v.y), h1, l1);
-          split_tf32(__uint_as_float(v.z), h2, l2);
-          split_tf32(__uint_as_float(v.w), h3, l3);
-          st_shared_v4(base + off, make_uint4(__float_as_uint(h0), __float_as_uint(h1), __float_as_uint(h2),
-                                              __float_as_uint(h3)));
-          st_shared_v4(base + lo_off, make_uint4(__float_as_uint(l0), __float_as_uint(l1), __float_as_uint(l2),
-                                                 __float_as_uint(l3)));
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(conv_bar + stage));
-        if (++stage == C::kStages) {
-          stage = 0;
-          phase ^= 1;
-        }
-      }
-    }
+    split_stages();
   } else if (warp >= 4) {
+    // Single-tile fp32 CTA: help split the stages first (the one accumulator
+    // cannot be ready before the last stage is split).
+    if (C::kTf32 && conv_warps == 6) split_stages();
     // ------------------------------------------------------------ epilogue
     using OutT = typename std::conditional<C::kTf32, float,
         typename std::conditional<kKind == kKindBf16, __nv_bfloat16, __half>::type>::type;

@@ -7,7 +7,10 @@ chunk the H2D copy of its A rows and B slices (copy stream 1), its grouped GEMM
 chained with events, so while chunk i is being multiplied chunk i+1 is
 uploading and chunk i-1 is downloading.  PCIe is full duplex, so a step costs
 about max(H2D bytes, D2H bytes) / PCIe bandwidth instead of their sum plus
-the GEMM.  Device buffers are double-buffered and reused across calls.
+the GEMM.  Device buffers are double-buffered and reused across calls.  Each
+chunk carries at least ``min_chunk_bytes`` of operands and output: a chunk
+costs a few microseconds of copy and launch latency (and tens of host
+microseconds), so a small problem moves in one piece.
 """
 
 from __future__ import annotations
@@ -28,10 +31,11 @@ def _chunks(bs: List[int], n_chunks: int) -> List[Tuple[int, int]]:
 class HostStreamedGmm:
     """Reusable pipeline state (streams, events, device buffers) for one device."""
 
-    def __init__(self, device=None, n_chunks: int = 8):
+    def __init__(self, device=None, n_chunks: int = 8, min_chunk_bytes: int = 32 << 20):
         self.device = torch.device("cuda", torch.cuda.current_device()) if device is None \
             else torch.device(device)
         self.n_chunks = n_chunks
+        self.min_chunk_bytes = min_chunk_bytes
         self.h2d = torch.cuda.Stream(self.device)
         self.d2h = torch.cuda.Stream(self.device)
         self._bufs = {}
@@ -59,7 +63,8 @@ class HostStreamedGmm:
         for m in bs:
             offs.append(offs[-1] + m)
         compute = torch.cuda.current_stream(self.device)
-        chunks = _chunks(bs, self.n_chunks)
+        total_bytes = (a.numel() + b.numel() + T * dim_out) * a.element_size()
+        chunks = _chunks(bs, max(1, min(self.n_chunks, total_bytes // max(1, self.min_chunk_bytes))))
         per_b = b[0].numel()
         max_rows = max(offs[e1] - offs[e0] for e0, e1 in chunks)
         max_e = max(e1 - e0 for e0, e1 in chunks)

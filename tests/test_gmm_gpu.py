@@ -270,8 +270,10 @@ def test_config_checksum_of_checksums(cid):
 @pytest.mark.parametrize("dtype,trans_b", [(torch.bfloat16, False), (torch.float16, True),
                                            (torch.float32, False)])
 def test_host_streamed_matches_device_op(dtype, trans_b):
-    """hopper_gmm_fwd_host (pipelined PCIe transfers) gives the device op's bytes."""
+    """hopper_gmm_fwd_host (pipelined PCIe transfers) gives the device op's bytes,
+    in one piece (the default for a problem this small) and cut into chunks."""
     from gmm_b200 import hopper_gmm_fwd, hopper_gmm_fwd_host
+    from gmm_b200.streaming import HostStreamedGmm
     g = torch.Generator().manual_seed(9)
     bs = torch.tensor([300, 0, 17, 512, 1, 0, 260, 99, 4])
     T, dim, dim_out = int(bs.sum()), 256, 384
@@ -279,8 +281,12 @@ def test_host_streamed_matches_device_op(dtype, trans_b):
     shape = (len(bs), dim_out, dim) if trans_b else (len(bs), dim, dim_out)
     b = (torch.randn(*shape, generator=g) / 16).to(dtype).pin_memory()
     want = hopper_gmm_fwd(a.cuda(), b.cuda(), bs, trans_b=trans_b).cpu()
+    chunked = HostStreamedGmm(n_chunks=4, min_chunk_bytes=1)
     for _ in range(2):  # the second call reuses the pipeline's buffers
         got = hopper_gmm_fwd_host(a, b, bs, trans_b=trans_b)
+        torch.cuda.synchronize()
+        assert torch.equal(got, want)
+        got = chunked(a, b, bs, trans_b)
         torch.cuda.synchronize()
         assert torch.equal(got, want)
 
