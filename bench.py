@@ -253,6 +253,39 @@ def _events_time(fn, steps, flush=None):
     return [s_.elapsed_time(e) for s_, e in zip(starts, ends)]
 
 
+def _pcie_bound(src_h, dst_h, h2d_bytes, d2h_bytes):
+    """The e2e step's transfer bound on this box: one large pinned-host copy each
+    way (from ``src_h``, into ``dst_h``), timed alone (CUDA events, median of
+    3), and the step's bytes over those rates.  A full-duplex link overlaps the
+    two directions, so the bound is the slower direction's time."""
+    import torch
+    n = min(src_h.numel(), dst_h.numel(), (256 << 20) // src_h.element_size())
+    h = src_h.reshape(-1)[:n]
+    o = dst_h.reshape(-1)[:n]
+    d = torch.empty(n, dtype=h.dtype, device="cuda")
+
+    def rate(fn):
+        fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(3):
+            s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s_.record()
+            fn()
+            e_.record()
+            torch.cuda.synchronize()
+            ts.append(s_.elapsed_time(e_))
+        return n * h.element_size() / (statistics.median(ts) * 1e-3) / 1e9
+
+    h2d_gbs = rate(lambda: d.copy_(h, non_blocking=True))
+    d2h_gbs = rate(lambda: o.copy_(d, non_blocking=True))
+    bound_ms = max(h2d_bytes / h2d_gbs, d2h_bytes / d2h_gbs) / 1e6
+    del d
+    return {"h2d_gbs": round(h2d_gbs, 1), "d2h_gbs": round(d2h_gbs, 1), "bound_ms": round(bound_ms, 3),
+            "note": "pinned-host copy rates measured alone on this box (256 MB each way); bound = the "
+                    "slower direction's bytes / rate"}
+
+
 DENSE_FLOP_PER_CLK = 148 * 8192  # B200: 148 SMs x 4096 bf16/fp16 FMA per clock each (dense)
 
 
@@ -388,6 +421,7 @@ def run_single(args):
     es = a.element_size()
     h2d = (a.numel() + b.numel()) * es
     d2h = cfg.rows * cfg.dim_out * es
+    pcie = _pcie_bound(b_h, d_h, h2d, d2h)
 
     if cfg.dtype == torch.float32 or cid in (3, 4):
         bound, achieved, peak, unit = "hbm", alg_bytes / (step_ms * 1e-3) / 1e9, peaks["hbm_gbs"], "GB/s"
@@ -429,7 +463,7 @@ def run_single(args):
         "parity": parity,
         "e2e": {"value": round(flops / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
                 "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": int(h2d),
-                "d2h_bytes_per_step": int(d2h),
+                "d2h_bytes_per_step": int(d2h), "pcie": pcie,
                 "path": "gmm_b200.hopper_gmm_fwd_host: pinned host A,B -> device, GEMM, "
                         "D -> pinned host, pipelined per expert chunk on 3 streams"},
         "gpu_launches": args.steps * launches_per_step,
