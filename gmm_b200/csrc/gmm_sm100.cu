@@ -62,7 +62,7 @@ constexpr int kMBlock = 16;          // m-tiles per raster block (L2 reuse of B 
 constexpr int kThreads = 256;        // 8 warps: TMA, MMA, TMEM alloc, idle, 4x epilogue
 constexpr int kEpiStageBytes = 4 * 32 * 128;  // epilogue staging: 4 warps x 32 rows x 128 B
 
-struct __align__(64) GmmParams {
+struct __align__(64) GmmParamsBase {
   CUtensorMap tmap_a;   // A, or A_hi for fp32
   CUtensorMap tmap_b;   // B, or B_hi for fp32
   CUtensorMap tmap_a2;  // A_lo (fp32 only)
@@ -98,6 +98,17 @@ struct __align__(64) GmmParams {
   unsigned long long wait_ns;
   int drop_kb1;
   void* d_peer[kMaxPeers];  // each rank's output buffer (remote mode)
+  int inline_ints;          // ints of inline_table in use (0: the table is in ext_table or built on device)
+};
+
+// Kernel parameters: the fields above plus the inline table, in two sizes.  A
+// launch copies the whole parameter block, and the full one (12 KB of table)
+// measured ~1 us slower per launch than a 1.5 KB one, so the 128-row and
+// swap-AB kernels are also instantiated with the small table, which every
+// call with at most kSmallGroups groups (or a table outside the parameters)
+// uses.
+template <int kTableInts>
+struct GmmParamsT : GmmParamsBase {
   // Table of the non-empty groups, laid out as
   //   row_off[G+1] | tile_off[G+1] | expert[G] [| src_off[G][W+1] | dst_row[G][W]]
   // row_off: first row of group g in A/D (row_off[G] = T);
@@ -105,8 +116,12 @@ struct __align__(64) GmmParams {
   // expert: index of the expert (B slice) of group g;
   // remote mode only -- src_off: where each source rank's rows start inside
   // group g; dst_row: the row on that source where they go back to.
-  int32_t inline_table[kInlineTableInts];
+  int32_t inline_table[kTableInts];
 };
+constexpr int kSmallGroups = 128;
+constexpr int kSmallTableInts = 3 * kSmallGroups + 2;
+using GmmParams = GmmParamsT<kInlineTableInts>;
+using GmmParamsSmall = GmmParamsT<kSmallTableInts>;
 
 enum Kind : int { kKindTf32x3 = 0, kKindBf16 = 1, kKindF16 = 2 };
 
@@ -143,7 +158,7 @@ struct TableView {
   const int32_t* dst_row;  // remote mode
 };
 
-__device__ __forceinline__ TableView make_table_view(const GmmParams& p, const int32_t* tab,
+__device__ __forceinline__ TableView make_table_view(const GmmParamsBase& p, const int32_t* tab,
                                                      int num_groups) {
   TableView tv;
   tv.row_off = tab;
@@ -190,7 +205,7 @@ __device__ __forceinline__ void block_scan3(long long (&v)[3], long long (&tot)[
 // above rows_cap (however large the sizes), leaves an empty table and an
 // error status, so no row past rows_cap is ever addressed.  After that check
 // every prefix fits in 32 bits (rows_cap < 2^31 - 256).
-__device__ void build_device_table(const GmmParams& p, int32_t* tab, int32_t* meta, long long* scratch) {
+__device__ void build_device_table(const GmmParamsBase& p, int32_t* tab, int32_t* meta, long long* scratch) {
   const int E = p.dev_experts;
   const int BM = p.tile_rows;
   constexpr int kPer = kMaxDevExperts / kThreads;  // experts per thread (4)
@@ -248,7 +263,7 @@ __device__ void build_device_table(const GmmParams& p, int32_t* tab, int32_t* me
 // Where output row `row` (a row of A, inside group g) is stored: D itself, or
 // in remote mode the output buffer of the rank the row came from.
 template <typename T>
-__device__ __forceinline__ T* out_row(const GmmParams& p, const TableView& tv, int g, int row) {
+__device__ __forceinline__ T* out_row(const GmmParamsBase& p, const TableView& tv, int g, int row) {
   if (!p.remote) return reinterpret_cast<T*>(p.d) + static_cast<long long>(row) * p.ldd;
   const int grow = row - tv.row_off[g];
   const int32_t* so = tv.src_off + g * (p.world + 1);
@@ -378,7 +393,7 @@ __device__ __forceinline__ void drain_rows(OutT* const (&rp)[8], int n0, int dim
 
 // drain_rows for a slab of grouped-GEMM rows: destinations from out_row().
 template <typename OutT, int BN>
-__device__ __forceinline__ void drain_slab(const GmmParams& p, const TableView& tv, int g,
+__device__ __forceinline__ void drain_slab(const GmmParamsBase& p, const TableView& tv, int g,
                                            int slab_row0, int slab_rows, int n0, uint32_t taddr,
                                            uint32_t stage, int lane) {
   OutT* rp[8];
@@ -396,7 +411,7 @@ __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f +
 // projections and [128, 256) the matching up projections; writes
 // silu(gate) * up (fp32) rounded to the output type, 128 columns per tile.
 template <typename OutT>
-__device__ __forceinline__ void drain_slab_swiglu(const GmmParams& p, const TableView& tv, int g,
+__device__ __forceinline__ void drain_slab_swiglu(const GmmParamsBase& p, const TableView& tv, int g,
                                                   int slab_row0, int slab_rows, int n0, uint32_t taddr,
                                                   uint32_t stage, int lane) {
   static_assert(sizeof(OutT) == 2, "SwiGLU epilogue is 16-bit");
@@ -456,8 +471,8 @@ __device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
   }
 }
 
-template <int kKind, bool kBMnMajor>
-__global__ void __launch_bounds__(kThreads, 1) gmm_persistent_kernel(const __grid_constant__ GmmParams p) {
+template <int kKind, bool kBMnMajor, typename P = GmmParams>
+__global__ void __launch_bounds__(kThreads, 1) gmm_persistent_kernel(const __grid_constant__ P p) {
   using C = Cfg<kKind, kBMnMajor>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -969,19 +984,51 @@ int encode(CUtensorMap* m, CUtensorMapDataType type, int rank, const void* ptr,
   return GMM_OK;
 }
 
-template <int kKind, bool kMn>
-int launch_variant(const GmmParams& prm, int grid, cudaStream_t stream, DeviceInfo* di, int bit) {
-  using C = Cfg<kKind, kMn>;
-  auto kern = gmm_persistent_kernel<kKind, kMn>;
+// Launch one instantiation of a kernel with its shared-memory attribute set
+// once per device (bit `bit` of smem_attr_set).
+template <typename P>
+int launch_with(void (*kern)(P), const P& prm, int grid, int smem, cudaStream_t stream, DeviceInfo* di, int bit,
+                const char* what) {
   if (!(di->smem_attr_set.load() & (1u << bit))) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
     di->smem_attr_set.fetch_or(1u << bit);
   }
-  kern<<<grid, kThreads, C::kSmemBytes, stream>>>(prm);
+  kern<<<grid, kThreads, smem, stream>>>(prm);
   cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "gmm kernel launch");
+  if (e != cudaSuccess) return cuda_fail(e, what);
   return GMM_OK;
+}
+
+// The small-table copy of `prm`, when its inline table (if any) fits.
+bool small_params(const GmmParams& prm, GmmParamsSmall& sp) {
+  if (prm.inline_ints > kSmallTableInts) return false;
+  static_cast<GmmParamsBase&>(sp) = static_cast<const GmmParamsBase&>(prm);
+  std::memcpy(sp.inline_table, prm.inline_table, static_cast<size_t>(prm.inline_ints) * sizeof(int32_t));
+  return true;
+}
+
+// A launch whose table travels in the parameters must say how much of it is
+// in use; anything else would hand the kernel a cut-off table.
+int check_table(const GmmParams& prm) {
+  if (prm.num_groups > 0 && prm.ext_table == nullptr && prm.dev_bs == nullptr &&
+      prm.inline_ints < 3 * prm.num_groups + 2)
+    return fail(GMM_ERR_INVALID_ARGUMENT, "internal: inline tile table size not set");
+  return GMM_OK;
+}
+
+// Small-table instantiations use bit + 16 of smem_attr_set (bits 0-15 are
+// taken by the full-table variants and the pair and variable-K kernels).
+template <int kKind, bool kMn>
+int launch_variant(const GmmParams& prm, int grid, cudaStream_t stream, DeviceInfo* di, int bit) {
+  using C = Cfg<kKind, kMn>;
+  if (int rc = check_table(prm)) return rc;
+  GmmParamsSmall sp;
+  if (small_params(prm, sp))
+    return launch_with(gmm_persistent_kernel<kKind, kMn, GmmParamsSmall>, sp, grid, C::kSmemBytes, stream, di,
+                       bit + 16, "gmm kernel launch");
+  return launch_with(gmm_persistent_kernel<kKind, kMn>, prm, grid, C::kSmemBytes, stream, di, bit,
+                     "gmm kernel launch");
 }
 
 // Launch the CTA-pair kernel: clusters of 2 CTAs, as many pairs as can be
@@ -1021,16 +1068,13 @@ int launch_pair(const GmmParams& prm, int total_tiles, cudaStream_t stream, Devi
 template <int kKind, bool kMn>
 int launch_swap(const GmmParams& prm, int grid, cudaStream_t stream, DeviceInfo* di, int bit) {
   using C = SwapCfg<kKind, kMn>;
-  auto kern = gmm_swap_kernel<kKind, kMn>;
-  if (!(di->smem_attr_set.load() & (1u << bit))) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(swap)");
-    di->smem_attr_set.fetch_or(1u << bit);
-  }
-  kern<<<grid, kThreads, C::kSmemBytes, stream>>>(prm);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "gmm swap kernel launch");
-  return GMM_OK;
+  if (int rc = check_table(prm)) return rc;
+  GmmParamsSmall sp;
+  if (small_params(prm, sp))
+    return launch_with(gmm_swap_kernel<kKind, kMn, GmmParamsSmall>, sp, grid, C::kSmemBytes, stream, di, bit + 16,
+                       "gmm swap kernel launch");
+  return launch_with(gmm_swap_kernel<kKind, kMn>, prm, grid, C::kSmemBytes, stream, di, bit,
+                     "gmm swap kernel launch");
 }
 
 // Tile kind of a problem.  fp32: 128-row tiles.  16-bit: CTA-pair 256-row
@@ -1294,6 +1338,7 @@ int launch_impl(const PlanObj& po, const Plan& pl, const void* A, const void* B,
   }
   if (pl.table_bytes == 0) {
     std::memcpy(prm.inline_table, pl.table.data(), pl.table.size() * sizeof(int32_t));
+    prm.inline_ints = static_cast<int>(pl.table.size());
     prm.ext_table = nullptr;
   } else {
     ce = cudaMemcpyAsync(workspace, pl.table.data(), pl.table.size() * sizeof(int32_t), cudaMemcpyHostToDevice,
@@ -1775,6 +1820,7 @@ extern "C" int gmm_sm100_forward_f32_noalloc(const float* A, const float* B,
   prm.tile_rows = 128;
   if (pl.table_bytes == 0) {
     std::memcpy(prm.inline_table, pl.table.data(), pl.table.size() * sizeof(int32_t));
+    prm.inline_ints = static_cast<int>(pl.table.size());
   } else {
     // The table is written in full (stream-ordered) before the kernel reads it.
     void* scratch = nullptr;

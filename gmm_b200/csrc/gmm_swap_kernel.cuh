@@ -90,8 +90,8 @@ __device__ __forceinline__ __nv_bfloat16 to_out<__nv_bfloat16>(float v) { return
 template <>
 __device__ __forceinline__ __half to_out<__half>(float v) { return __float2half_rn(v); }
 
-template <int kKind, bool kBMnMajor>
-__global__ void __launch_bounds__(kThreads, 1) gmm_swap_kernel(const __grid_constant__ GmmParams p) {
+template <int kKind, bool kBMnMajor, typename P = GmmParams>
+__global__ void __launch_bounds__(kThreads, 1) gmm_swap_kernel(const __grid_constant__ P p) {
   using C = SwapCfg<kKind, kBMnMajor>;
   constexpr int kCols = C::kCols;
   using OutT = typename std::conditional<kKind == kKindBf16, __nv_bfloat16, __half>::type;
