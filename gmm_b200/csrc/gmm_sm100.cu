@@ -30,6 +30,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
+#include <nvtx3/nvToolsExt.h>
 
 #include <algorithm>
 #include <atomic>
@@ -851,6 +852,16 @@ using namespace gmm_sm100;
 
 thread_local std::string t_last_error;
 
+// NVTX range around the host half of an entry point (plan building, tensor
+// maps, launch): shows in Nsight Systems / Compute timelines next to the
+// kernels it enqueues; without an attached tool it costs a few nanoseconds.
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange&) = delete;
+  NvtxRange& operator=(const NvtxRange&) = delete;
+};
+
 int fail(int code, const std::string& msg) {
   t_last_error = msg;
   return code;
@@ -1238,6 +1249,7 @@ struct PlanObj {
 
 int plan_impl(const int64_t* batch_sizes, int64_t num_experts, int64_t num_tokens, int64_t dim,
               int64_t dim_out, int dtype, int trans_b, int act, bool remote, PlanObj& po) {
+  NvtxRange range("gmm_sm100 plan");
   int rc = make_plan(batch_sizes, num_experts, num_tokens, dim, dim_out, dtype, po.pl);
   if (rc != GMM_OK) return rc;
   po.kind = choose_tile_kind(batch_sizes, num_experts, num_tokens, dtype, act, remote);
@@ -1265,6 +1277,7 @@ struct InjectTimeout {
 int launch_impl(const PlanObj& po, const Plan& pl, const void* A, const void* B, void* D, void* workspace,
                 size_t workspace_bytes, void* stream_ptr, const EpRoute* ep, int act,
                 const InjectTimeout* inject = nullptr) {
+  NvtxRange range("gmm_sm100 launch");
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
   int rc = GMM_OK;
   const TileKind kind = po.kind;
@@ -1479,6 +1492,7 @@ int gmm_sm100_forward_ep(const void* X, const void* B, const int64_t* counts, co
 int gmm_sm100_ep_gather(void* X, const void* const* src_peers, const int64_t* counts,
                         const int64_t* src_rows, int64_t num_local_experts, int world, int rank_base,
                         int64_t row_bytes, void* stream_ptr) {
+  NvtxRange range("gmm_sm100 ep_gather");
   if (!counts || !src_rows || !src_peers || world < 1 || world > kMaxPeers || num_local_experts < 0)
     return fail(GMM_ERR_INVALID_ARGUMENT, "bad gather arguments");
   if (row_bytes <= 0 || row_bytes % 16 != 0)
@@ -1531,6 +1545,7 @@ int gmm_sm100_ep_gather(void* X, const void* const* src_peers, const int64_t* co
 
 int gmm_sm100_ep_barrier(int* const* flag_peers, int world, int rank, int epoch, double timeout_s,
                          void* stream_ptr) {
+  NvtxRange range("gmm_sm100 ep_barrier");
   if (!flag_peers || world < 1 || world > kMaxPeers || rank < 0 || rank >= world || !(timeout_s > 0.0))
     return fail(GMM_ERR_INVALID_ARGUMENT, "bad barrier arguments");
   BarrierParams prm;
@@ -1565,6 +1580,7 @@ size_t gmm_sm100_dev_workspace_size(int64_t num_experts, int64_t rows_cap, int64
 int gmm_sm100_forward_dev(const void* A, const void* B, const int32_t* batch_sizes_dev, int64_t num_experts,
                           int64_t rows_cap, int64_t dim, int64_t dim_out, int dtype, int trans_b, int swiglu,
                           void* D, void* workspace, size_t workspace_bytes, void* stream_ptr) {
+  NvtxRange range("gmm_sm100 forward_dev");
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
   if (num_experts < 1 || num_experts > kMaxDevExperts || rows_cap < 0 || dim < 0 || dim_out < 0)
     return fail(GMM_ERR_INVALID_ARGUMENT, "device batch sizes need 1 <= num_experts <= 1024");
@@ -1776,6 +1792,7 @@ extern "C" int gmm_sm100_forward_f32_noalloc(const float* A, const float* B,
                                              const int64_t* batch_sizes, int64_t num_experts,
                                              int64_t num_tokens, int64_t dim, int64_t dim_out,
                                              int trans_b, float* D, void* stream_ptr) {
+  NvtxRange range("gmm_sm100 forward_f32_noalloc");
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
   Plan pl;
   int rc = make_plan(batch_sizes, num_experts, num_tokens, dim, dim_out, GMM_DTYPE_F32, pl);

@@ -412,7 +412,11 @@ class ExpertParallelGmm:
                                 or out.dtype != a.dtype or out.device != a.device):
             raise ValueError("out must be a [T_r, dim_out] tensor of a's dtype and device")
         if self._use_direct(a):
-            return self._forward_direct(a, b_local, all_bs, trans_b, out)
+            torch.cuda.nvtx.range_push("gmm_b200 ep forward (direct)")  # Nsight timeline marker
+            try:
+                return self._forward_direct(a, b_local, all_bs, trans_b, out)
+            finally:
+                torch.cuda.nvtx.range_pop()
         bs = all_bs.tolist()
         ch = _Chunking(bs, W, El, self.chunks)
         C = ch.chunks
