@@ -115,6 +115,28 @@ def test_more_groups_than_inline_table():
     assert ok, (nbad, err)
 
 
+@pytest.mark.parametrize("groups", [127, 128, 129, 1024, 1025])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_table_size_boundaries(groups, dtype, tile):
+    """Non-empty expert counts either side of the two inline-table sizes (128
+    groups travel in the small parameter block, up to 1024 in the full one,
+    more in the workspace): every kernel family gets its whole table."""
+    g = torch.Generator().manual_seed(groups)
+    bs = torch.randint(1, 4, (groups + groups // 9,), generator=g)
+    bs[torch.randperm(bs.numel(), generator=g)[:groups // 9]] = 0  # empty experts between the others
+    assert int((bs > 0).sum()) == groups
+    T, dim, dim_out = int(bs.sum()), 64, 96
+    a = torch.randn(T, dim, generator=g).to(dtype)
+    b = (torch.randn(bs.numel(), dim, dim_out, generator=g) / 8).to(dtype)
+    out = _fwd(a.cuda(), b.cuda(), bs, False)
+    name = oracle.dtype_name(dtype)
+    want = oracle.gmm_oracle_np(a, b, bs, False)
+    if dtype != torch.float32:
+        want = oracle.round_to(want, name)
+    ok, nbad, err = oracle.allclose_report(out.float().cpu().numpy(), want, oracle.TOLERANCE[name])
+    assert ok, (groups, nbad, err)
+
+
 def test_degenerate_sizes(tile):
     dev = "cuda"
     # all experts empty -> T = 0
