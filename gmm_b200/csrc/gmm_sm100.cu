@@ -64,10 +64,9 @@ constexpr int kThreads = 256;        // 8 warps: TMA, MMA, TMEM alloc, idle, 4x 
 constexpr int kEpiStageBytes = 4 * 32 * 128;  // epilogue staging: 4 warps x 32 rows x 128 B
 
 struct __align__(64) GmmParamsBase {
-  CUtensorMap tmap_a;   // A, or A_hi for fp32
-  CUtensorMap tmap_b;   // B, or B_hi for fp32
-  CUtensorMap tmap_a2;  // A_lo (fp32 only)
-  CUtensorMap tmap_b2;  // B_lo (fp32 only)
+  CUtensorMap tmap_a;   // A (fp32: raw fp32 tiles, split into TF32 hi/lo in shared memory)
+  CUtensorMap tmap_b;   // B
+  CUtensorMap tmap_a2;  // A in 64-row boxes (half tiles of the CTA-pair kernel)
   void* d;
   const int32_t* ext_table;  // device table when num_groups > kInlineGroups
   long long ldd;
