@@ -28,6 +28,12 @@ def _chunks(bs: List[int], n_chunks: int) -> List[Tuple[int, int]]:
     return [(bounds[i], bounds[i + 1]) for i in range(n_chunks) if bounds[i + 1] > bounds[i]]
 
 
+def chunk_count(total_bytes: int, n_chunks: int, min_chunk_bytes: int) -> int:
+    """Chunks for a problem of ``total_bytes`` (operands + output): at most
+    ``n_chunks``, each carrying at least ``min_chunk_bytes``, at least one."""
+    return max(1, min(n_chunks, total_bytes // max(1, min_chunk_bytes)))
+
+
 class HostStreamedGmm:
     """Reusable pipeline state (streams, events, device buffers) for one device."""
 
@@ -64,7 +70,7 @@ class HostStreamedGmm:
             offs.append(offs[-1] + m)
         compute = torch.cuda.current_stream(self.device)
         total_bytes = (a.numel() + b.numel() + T * dim_out) * a.element_size()
-        chunks = _chunks(bs, max(1, min(self.n_chunks, total_bytes // max(1, self.min_chunk_bytes))))
+        chunks = _chunks(bs, chunk_count(total_bytes, self.n_chunks, self.min_chunk_bytes))
         per_b = b[0].numel()
         max_rows = max(offs[e1] - offs[e0] for e0, e1 in chunks)
         max_e = max(e1 - e0 for e0, e1 in chunks)

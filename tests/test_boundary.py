@@ -194,3 +194,23 @@ def test_tile_kind_override_roundtrip():
         assert capi.set_tile_kind("auto") == "256"
     finally:
         capi.set_tile_kind(prev)
+
+
+def test_host_pipeline_chunking():
+    """hopper_gmm_fwd_host moves a small problem in one piece and cuts a large
+    one into expert chunks of at least min_chunk_bytes each (host logic only)."""
+    from gmm_b200.configs import CONFIGS, batch_sizes_for
+    from gmm_b200.streaming import _chunks, chunk_count
+    mb = 1 << 20
+    assert chunk_count(2 * mb, 8, 32 * mb) == 1           # cfg1-sized: one chunk
+    assert chunk_count(0, 8, 32 * mb) == 1
+    assert chunk_count(100 * mb, 8, 32 * mb) == 3
+    assert chunk_count(1544 * mb, 8, 32 * mb) == 8        # cfg2-sized: the full pipeline
+    assert chunk_count(10 * mb, 8, 0) == 8                 # no floor: n_chunks
+    for cid in (1, 2, 3, 4, 5):
+        bs = [int(v) for v in batch_sizes_for(CONFIGS[cid]).tolist()]
+        for n in (1, 3, 8):
+            spans = _chunks(bs, n)
+            assert spans[0][0] == 0 and spans[-1][1] == len(bs)
+            assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+            assert 1 <= len(spans) <= n
