@@ -18,7 +18,6 @@ from __future__ import annotations
 
 from typing import Optional, Tuple
 
-import numpy as np
 import torch
 
 from gmm_b200 import capi

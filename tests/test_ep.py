@@ -8,7 +8,6 @@ and checks that the survivor fails with an error instead of hanging.
 
 import datetime
 import os
-import socket
 import tempfile
 
 import pytest

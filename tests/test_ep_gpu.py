@@ -5,7 +5,6 @@ from the same operands, only its neighbours in the tile differ."""
 
 import datetime
 import os
-import socket
 import tempfile
 
 import pytest

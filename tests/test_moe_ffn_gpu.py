@@ -5,7 +5,6 @@ The oracle applies silu(gate) * up to fp64 per-expert products and rounds
 once, which is what the fused epilogue does from its fp32 accumulators; the
 tolerances are the grouped GEMM's (bf16 1.6e-2, fp16 2e-3)."""
 
-import numpy as np
 import pytest
 import torch
 

@@ -3,7 +3,6 @@ D[e] = A[rows_e]^T @ B[rows_e].  Ragged row counts that are not multiples of the
 64-row contraction block make the kernel zero the next expert's rows in shared
 memory; empty experts must come out as exact zeros."""
 
-import numpy as np
 import pytest
 import torch
 
